@@ -1,0 +1,124 @@
+/*
+ * vmlx_cuda.h -- C ABI of the B200 (sm_100a) affine-quantized linear path.
+ *
+ * Drop-in device-side replacement for the entry points that vmlx-swift's
+ * QuantizedLinear / SwitchGLU / MLXDistributedTP layers reach through mlx-c
+ * and CmlxDistributedShim.  Every function:
+ *   - takes plain device pointers and sizes (no framework types);
+ *   - is stream ordered on the `stream` argument (a cudaStream_t passed as
+ *     void*, NULL = legacy default stream) and never synchronises the host,
+ *     so calls can be captured into a CUDA graph;
+ *   - allocates nothing on the hot path: outputs are caller-allocated;
+ *   - returns VMLX_OK (0) or a VMLX_E_* code and leaves a description in the
+ *     calling thread's vmlx_last_error() (the mlx-c convention of returning a
+ *     nonzero int plus an error handler, Source/Cmlx/include/mlx/c/error.h:15-33);
+ *   - never aborts the process and never waits without a bound.
+ *
+ * Tensor conventions (MLX affine layout, Source/MLX/Ops.swift:2368-2388):
+ *   x        bf16  [M, K]                (activations, row major)
+ *   w        u32   [N, K*bits/32]        (element k of row n at word k/(32/bits),
+ *                                          bit offset bits*(k%(32/bits)))
+ *   scales   bf16  [N, K/group_size]
+ *   biases   bf16  [N, K/group_size]
+ *   y        bf16  [M, N]                y = x @ dequantize(w)^T  (transpose=true)
+ * Supported: mode "affine" (or NULL), bits in {2,4,8}, group_size in {32,64,128},
+ * transpose = true (the only orientation the quantized layers use,
+ * Source/MLXNN/Quantized.swift:367, Libraries/MLXLMCommon/SwitchLayers.swift:500).
+ */
+#ifndef VMLX_CUDA_H
+#define VMLX_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VMLX_API __attribute__((visibility("default")))
+#else
+#define VMLX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VMLX_OK 0
+#define VMLX_E_INVALID 1      /* bad pointer, shape or argument */
+#define VMLX_E_UNSUPPORTED 2  /* bits / group_size / mode / transpose not supported */
+#define VMLX_E_CUDA 3         /* a CUDA runtime call failed */
+#define VMLX_E_PEER_TIMEOUT 4 /* a bounded wait on a peer GPU ran out */
+#define VMLX_E_STATE 5        /* handle used in the wrong state */
+
+/* Element types for the dtype arguments. */
+#define VMLX_BF16 0
+#define VMLX_F32 1
+
+/* Text of the last error raised on the calling thread ("" if none). */
+VMLX_API const char* vmlx_last_error(void);
+
+/* ABI version: major*10000 + minor*100 + patch. */
+VMLX_API int vmlx_version(void);
+
+/*
+ * Affine quantization of a row-major matrix w [rows, cols].
+ * Replaces mlx_quantize (Source/Cmlx/include/mlx/c/ops.h:801-808) for
+ * mode "affine"; arithmetic of affine_quantize
+ * (Source/Cmlx/mlx-generated/metal/quantized.h:2393-2496).
+ * w_dtype = VMLX_BF16 or VMLX_F32; scales/biases are written in the same dtype
+ * (MLX returns scales in the input dtype).
+ */
+VMLX_API int vmlx_cuda_quantize(void* wq, void* scales, void* biases, const void* w, int w_dtype,
+                       int64_t rows, int64_t cols, int group_size, int bits, const char* mode,
+                       void* stream);
+
+/*
+ * Affine dequantization: out[r, k] = scale*q + bias, computed in fp32 and
+ * stored as out_dtype (VMLX_F32: exact; VMLX_BF16: round to nearest even).
+ * Replaces mlx_dequantize (Source/Cmlx/include/mlx/c/ops.h:359-369);
+ * arithmetic of affine_dequantize (quantized.h:2498-2558).
+ * scales_dtype gives the dtype of scales/biases.
+ */
+VMLX_API int vmlx_cuda_dequantize(void* out, int out_dtype, const uint32_t* wq, const void* scales,
+                         const void* biases, int scales_dtype, int64_t rows, int64_t cols,
+                         int group_size, int bits, const char* mode, void* stream);
+
+/*
+ * y [M, N] = x [M, K] @ dequantize(w [N, K])^T, bf16 in/out, fp32 accumulation.
+ * Replaces mlx_quantized_matmul (Source/Cmlx/include/mlx/c/ops.h:809-819), the
+ * op behind QuantizedLinear.callAsFunction (Source/MLXNN/Quantized.swift:361-376).
+ * biases may not be NULL for mode "affine".  M <= 32 runs the decode GEMV
+ * kernel; larger M runs the tensor-core (tcgen05) GEMM.
+ */
+VMLX_API int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t* w, const void* scales,
+                               const void* biases, bool transpose, int group_size, int bits,
+                               const char* mode, int64_t M, int64_t N, int64_t K, void* stream);
+
+/*
+ * Gathered quantized matmul over a stack of E expert matrices.
+ * Replaces mlx_gather_qmm (Source/Cmlx/include/mlx/c/ops.h:475-488), the op
+ * behind QuantizedSwitchLinear.callAsFunction
+ * (Libraries/MLXLMCommon/SwitchLayers.swift:491-512).
+ *   x        bf16 [x_batches, M, K]
+ *   w        u32  [E, N, K*bits/32];  scales/biases bf16 [E, N, K/group_size]
+ *   lhs_indices u32 [batch] or NULL.  NULL means each x matrix serves
+ *               batch/x_batches consecutive batch elements (b reads x batch
+ *               b*x_batches/batch), the row-major broadcast of x [T,1,..]
+ *               against indices [T,k] that SwitchGLU relies on
+ *               (quantized.h:1438-1491); batch must be a multiple of x_batches.
+ *   rhs_indices u32 [batch]  expert of each batch element
+ *   y        bf16 [batch, M, N];  y[b] = x[lhs[b]] @ dequantize(w[rhs[b]])^T
+ * sorted_indices = true promises rhs_indices is non-decreasing (the
+ * gatherSort'ed order, SwitchLayers.swift:64-75); the kernel then streams each
+ * expert's weights once for the whole run of batch elements routed to it.
+ * Out-of-range expert ids (>= n_experts) produce zero rows.
+ */
+VMLX_API int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, const void* scales,
+                         const void* biases, const uint32_t* lhs_indices,
+                         const uint32_t* rhs_indices, bool transpose, int group_size, int bits,
+                         const char* mode, bool sorted_indices, int64_t batch, int64_t x_batches,
+                         int64_t M, int64_t N, int64_t K, int64_t n_experts, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VMLX_CUDA_H */

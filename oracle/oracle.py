@@ -1,0 +1,217 @@
+"""CPU oracle for the quantized-linear path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may use
+this module, and only as the checker / timed baseline.  The product library
+never calls it.
+
+Wraps oracle/libvmlxq_ref.so (the C restatement in vmlxq_ref.c of the MLX
+affine quantize / dequantize / qmv arithmetic, Source/Cmlx/mlx-generated/
+metal/quantized.h) and adds numpy restatements of the layer logic:
+  gather_sort / scatter_unsort / SwitchGLU  Libraries/MLXLMCommon/SwitchLayers.swift:64-83, 261-366
+  MoE routing                               Libraries/MLXLLM/Models/Qwen3MoE.swift:137-152
+  TP column/row sharding + allSum           Libraries/MLXDistributedTP/LinearLayers.swift:59-205
+Seeded inputs come from numpy's PCG64 generator (np.random.default_rng(seed)).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "libvmlxq_ref.so")
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        h = ctypes.CDLL(LIB)
+        P = ctypes.c_void_p
+        I64 = ctypes.c_int64
+        I = ctypes.c_int
+        h.vq_quantize_f32.argtypes = [P, I64, I64, I, I, P, P, P]
+        h.vq_quantize_bf16.argtypes = [P, I64, I64, I, I, P, P, P]
+        h.vq_dequantize.argtypes = [P, P, P, I, I64, I64, I, I, P]
+        h.vq_qmm_f64.argtypes = [P, I64, I64, P, P, P, I64, I, I, P]
+        h.vq_qmm_fp32.argtypes = [P, I64, I64, P, P, P, I64, I, I, P]
+        h.vq_gather_qmm_f64.argtypes = [P, I64, I64, P, P, P, I64, I64, P, P, I64, I, I, P]
+        h.vq_num_threads.restype = I
+        _lib = h
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---- bf16 helpers (bit patterns in uint16) ----------------------------------
+
+def f32_to_bf16(a) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bf16 bit patterns (uint16)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(h) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(a) -> np.ndarray:
+    return bf16_to_f32(f32_to_bf16(a))
+
+
+# ---- quantize / dequantize / matmul -----------------------------------------
+
+def quantize(w, group_size=64, bits=4, dtype="bf16"):
+    """Returns (wq uint32 [rows, K*bits/32], scales, biases) with scales/biases as
+    bf16 bit patterns (dtype='bf16'; w given as uint16 bit patterns or floats that
+    are first rounded to bf16) or float32 (dtype='f32')."""
+    w = np.asarray(w)
+    shape = w.shape
+    K = shape[-1]
+    rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+    wq = np.zeros((rows, K * bits // 32), np.uint32)
+    ng = K // group_size
+    if dtype == "bf16":
+        wb = w if w.dtype == np.uint16 else f32_to_bf16(w)
+        wb = np.ascontiguousarray(wb.reshape(rows, K))
+        s = np.zeros((rows, ng), np.uint16)
+        b = np.zeros((rows, ng), np.uint16)
+        rc = lib().vq_quantize_bf16(_p(wb), rows, K, group_size, bits, _p(wq), _p(s), _p(b))
+    else:
+        wf = np.ascontiguousarray(w.reshape(rows, K), dtype=np.float32)
+        s = np.zeros((rows, ng), np.float32)
+        b = np.zeros((rows, ng), np.float32)
+        rc = lib().vq_quantize_f32(_p(wf), rows, K, group_size, bits, _p(wq), _p(s), _p(b))
+    if rc:
+        raise ValueError(f"oracle quantize failed rc={rc}")
+    lead = shape[:-1]
+    return wq.reshape(*lead, -1), s.reshape(*lead, ng), b.reshape(*lead, ng)
+
+
+def dequantize(wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """Exact fp32 dequantization float(s)*q + float(b)."""
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    K = wq.shape[-1] * 32 // bits
+    rows = wq.size // wq.shape[-1]
+    is_bf16 = scales.dtype == np.uint16
+    s = np.ascontiguousarray(scales)
+    b = np.ascontiguousarray(biases)
+    out = np.zeros((rows, K), np.float32)
+    rc = lib().vq_dequantize(_p(wq), _p(s), _p(b), int(is_bf16), rows, K, group_size, bits, _p(out))
+    if rc:
+        raise ValueError("oracle dequantize failed")
+    return out.reshape(*wq.shape[:-1], K)
+
+
+def qmm_f64(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """fp64-accumulated y = x @ deq(W)^T; x given as bf16 bit patterns [M, K]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    M, K = x.shape
+    N = wq.shape[0]
+    y = np.zeros((M, N), np.float64)
+    rc = lib().vq_qmm_f64(_p(x), M, K, _p(np.ascontiguousarray(wq, np.uint32)),
+                          _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                          N, group_size, bits, _p(y))
+    if rc:
+        raise ValueError("oracle qmm failed")
+    return y
+
+
+def qmm_fp32_bf16(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """MLX-factorised fp32 GEMV (OpenMP), bf16 bit-pattern output [M, N]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    M, K = x.shape
+    N = wq.shape[0]
+    y = np.zeros((M, N), np.uint16)
+    rc = lib().vq_qmm_fp32(_p(x), M, K, _p(np.ascontiguousarray(wq, np.uint32)),
+                           _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                           N, group_size, bits, _p(y))
+    if rc:
+        raise ValueError("oracle qmm_fp32 failed")
+    return y
+
+
+def gather_qmm_f64(x_bf16, wq, scales, biases, lhs, rhs, group_size=64, bits=4) -> np.ndarray:
+    """y[b] = x[lhs[b]] @ deq(W[rhs[b]])^T in fp64 (quantized.h:1438-1491 semantics).
+
+    x [xb, M, K] bf16 bits; W [E, N, K/pf].  lhs None: batch b reads x batch
+    b*xb/nb.  Each routed expert is dequantized once (C oracle, exact fp32) and
+    all batch elements routed to it are multiplied in one fp64 matmul."""
+    x = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16)).astype(np.float64)
+    xb, M, K = x.shape
+    E, N = wq.shape[0], wq.shape[1]
+    rhs = np.asarray(rhs, dtype=np.int64).reshape(-1)
+    nb = rhs.size
+    lhs_a = (np.arange(nb) * xb // max(nb, 1)) if lhs is None else np.asarray(lhs, np.int64).reshape(-1)
+    y = np.zeros((nb, M, N), np.float64)
+    for e in np.unique(rhs):
+        if e < 0 or e >= E:
+            continue
+        sel = np.nonzero(rhs == e)[0]
+        w = dequantize(wq[e], scales[e], biases[e], group_size, bits).astype(np.float64)
+        y[sel] = np.einsum("bmk,nk->bmn", x[lhs_a[sel]], w)
+    return y
+
+
+def num_threads() -> int:
+    return lib().vq_num_threads()
+
+
+# ---- layer logic (numpy) -----------------------------------------------------
+
+def gather_sort(indices: np.ndarray):
+    """Order / sorted indices / inverse order of SwitchLayers.swift:64-75 (stable)."""
+    flat = indices.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    inv = np.argsort(order, kind="stable")
+    return order, flat[order], inv
+
+
+def silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def switch_glu(x_bf16, gate, up, down, indices, group_size=64, bits=4) -> np.ndarray:
+    """Reference SwitchGLU forward: x [T, D] bf16 bits, indices [T, k];
+    gate/up/down = (wq, scales, biases) stacks.  Returns float64 [T, k, D].
+    Intermediate activations are rounded to bf16 where the reference holds
+    bf16 arrays (gate/up outputs, silu(g)*u)."""
+    T, D = x_bf16.shape
+    k = indices.shape[1]
+    rhs = indices.reshape(-1).astype(np.uint32)
+    xb = x_bf16.reshape(T, 1, D)
+    lhs = np.repeat(np.arange(T), k).astype(np.uint32)
+    g = round_bf16(gather_qmm_f64(xb, *gate, lhs, rhs, group_size, bits).astype(np.float32))
+    u = round_bf16(gather_qmm_f64(xb, *up, lhs, rhs, group_size, bits).astype(np.float32))
+    act = f32_to_bf16(round_bf16(silu(g.astype(np.float64)).astype(np.float32)) * u)
+    y = gather_qmm_f64(act.reshape(T * k, 1, -1), *down, None, rhs, group_size, bits)
+    return y.reshape(T, k, -1)
+
+
+def moe_route(logits: np.ndarray, k: int, norm_topk_prob: bool = False):
+    """softmax(precise) -> top-k expert ids (as a sorted set per token) and scores
+    (Qwen3MoE.swift:137-152).  The reference's order inside the top-k is
+    implementation-defined, so ids are returned sorted ascending."""
+    z = logits.astype(np.float64)
+    z = np.exp(z - z.max(-1, keepdims=True))
+    p = z / z.sum(-1, keepdims=True)
+    top = np.argsort(-p, axis=-1, kind="stable")[:, :k]
+    top = np.sort(top, axis=-1)
+    sc = np.take_along_axis(p, top, -1)
+    if norm_topk_prob:
+        sc = sc / sc.sum(-1, keepdims=True)
+    return top.astype(np.uint32), sc

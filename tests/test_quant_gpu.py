@@ -1,0 +1,200 @@
+"""GPU parity of quantize / dequantize / quantized_mm / gather_qmm / SwitchGLU
+against the CPU oracle, through the C ABI.
+
+Bars: packed words and bf16 scale/bias bit patterns are bit-exact; fp32
+dequantization is bit-exact; matmul outputs (fp32 accumulation, bf16 out)
+satisfy max |err| / max |ref| <= 1e-2 and mean |err| / mean |ref| <= 1e-3
+against the fp64 oracle (the tolerance stated in BASELINE.json north_star)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-2
+MEAN_REL = 1e-3
+
+
+def to_dev_bf16(orc, a_bits, dev):
+    return torch.from_numpy(a_bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+
+
+def bits_of(t):
+    return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def u32(t):
+    return t.detach().cpu().numpy().view(np.uint32)
+
+
+def check_close(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref)
+    scale_max = np.abs(ref).max() + 1e-30
+    scale_mean = np.abs(ref).mean() + 1e-30
+    assert err.max() / scale_max <= MAX_REL, (err.max(), scale_max)
+    assert err.mean() / scale_mean <= MEAN_REL, (err.mean(), scale_mean)
+
+
+def make_weights(orc, vm, dev, N, K, gs, bits, seed, lead=()):
+    rng = np.random.default_rng(seed)
+    w32 = rng.normal(0, 0.02, (*lead, N, K)).astype(np.float32)
+    wb = orc.f32_to_bf16(w32)
+    wt = to_dev_bf16(orc, wb, dev)
+    wq, s, b = vm.quantized(wt, group_size=gs, bits=bits)
+    return wb, (wq, s, b)
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_quantize_bit_exact_bf16(vm, orc, cuda, bits, gs):
+    rng = np.random.default_rng(bits * 100 + gs)
+    w = rng.normal(0, 0.02, (96, 8 * gs)).astype(np.float32)
+    w[0, :gs] = -np.abs(w[0, :gs])
+    w[1, :gs] = 0
+    w[2, :gs] = 0.125
+    w[3, gs:2 * gs] = np.linspace(-1, 3, gs)
+    wb = orc.f32_to_bf16(w)
+    wq, s, b = vm.quantized(to_dev_bf16(orc, wb, cuda), group_size=gs, bits=bits)
+    rq, rs, rb = orc.quantize(wb, gs, bits, dtype="bf16")
+    assert np.array_equal(u32(wq), rq)
+    assert np.array_equal(bits_of(s), rs)
+    assert np.array_equal(bits_of(b), rb)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantize_bit_exact_f32(vm, orc, cuda, bits):
+    rng = np.random.default_rng(7)
+    w = rng.uniform(0, 1, (32, 256)).astype(np.float32)  # IntegrationTests.swift:3890 shape
+    wq, s, b = vm.quantized(torch.from_numpy(w).to(cuda), group_size=64, bits=bits)
+    rq, rs, rb = orc.quantize(w, 64, bits, dtype="f32")
+    assert np.array_equal(u32(wq), rq)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(b.cpu().numpy().view(np.uint32), rb.view(np.uint32))
+    assert s.dtype == torch.float32 and wq.shape == (32, 256 * bits // 32)
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_dequantize_bit_exact(vm, orc, cuda, bits):
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, 64, 512, 64, bits, 11)
+    ref = orc.dequantize(u32(wq), bits_of(s), bits_of(b), 64, bits)
+    got32 = vm.dequantized(wq, s, b, 64, bits, dtype=torch.float32).cpu().numpy()
+    assert np.array_equal(got32.view(np.uint32), ref.view(np.uint32))
+    got16 = bits_of(vm.dequantized(wq, s, b, 64, bits, dtype=torch.bfloat16))
+    assert np.array_equal(got16, orc.f32_to_bf16(ref))
+
+
+def test_known_answer_fixture_gpu(vm, orc, cuda):
+    """QuantizationTests.swift:65-111 on the GPU path (float32 weights, gs 32, b4)."""
+    dense = (np.arange(3 * 16 * 32, dtype=np.float32).reshape(3, 16, 32) / 2048) - 0.5
+    x = (np.arange(2 * 1 * 32, dtype=np.float32).reshape(2, 1, 32) / 128) - 0.25
+    wq, s, b = vm.quantized(torch.from_numpy(dense).to(cuda), group_size=32, bits=4)
+    rq, rs, rb = orc.quantize(dense, 32, 4, dtype="f32")
+    assert np.array_equal(u32(wq), rq)
+    deq = vm.dequantized(wq, s, b, 32, 4, dtype=torch.float32).cpu().numpy()
+    # the gather path takes bf16 scales; use the bf16-quantized weights
+    wqb, sb, bb = vm.quantized(torch.from_numpy(dense).to(cuda).bfloat16(), group_size=32, bits=4)
+    xt = torch.from_numpy(x).to(cuda).bfloat16()
+    got = vm.gather_quantized_mm(xt, wqb, sb, bb, rhs_indices=torch.tensor([0, 2], device=cuda),
+                                 group_size=32, bits=4).float().cpu().numpy()
+    deqb = vm.dequantized(wqb, sb, bb, 32, 4, dtype=torch.float32).cpu().numpy()
+    expected = np.concatenate([x[0] @ deqb[0].T, x[1] @ deqb[2].T], 0)
+    np.testing.assert_allclose(got.reshape(2, 16), expected, rtol=1e-2, atol=2e-3)
+    np.testing.assert_allclose(deq, orc.dequantize(rq, rs, rb, 32, 4))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M", [1, 3, 8, 13, 32])
+def test_quantized_mm_gemv(vm, orc, cuda, bits, gs, M):
+    N, K = 272, 1024 + 2 * gs   # N not a multiple of 16, K not a multiple of 8 groups
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, gs, bits, 21 + M)
+    rng = np.random.default_rng(5 + M)
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
+    y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=gs, bits=bits)
+    ref = orc.qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), gs, bits)
+    check_close(y.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("M", [1, 8, 32, 128, 512])
+def test_quantized_mm_llama_ffn_shapes(vm, orc, cuda, M):
+    """BASELINE config 2 shapes (4096->14336 and 14336->4096), 4-bit g64."""
+    for (K, N) in [(4096, 14336), (14336, 4096)]:
+        wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 31)
+        rng = np.random.default_rng(9)
+        xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
+        y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=64, bits=4)
+        rows = np.arange(0, N, 37)  # the fp64 oracle on a sample of output columns
+        ref = orc.qmm_f64(xb, u32(wq)[rows], bits_of(s)[rows], bits_of(b)[rows], 64, 4)
+        check_close(y.float().cpu().numpy()[:, rows], ref)
+
+
+def test_batch_invariance(vm, orc, cuda):
+    """QuantizedSmallMScalingBenchTests.swift:110-127: M rows at once must equal
+    M single-row calls exactly (maxDiff == 0), 4-bit g64 bf16."""
+    K, N = 5120, 1024
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 41)
+    x = torch.randn(32, K, device=cuda, generator=torch.Generator(cuda).manual_seed(0)).bfloat16()
+    for M in (4, 16, 32):
+        full = vm.quantized_mm(x[:M], wq, s, b)
+        singles = torch.cat([vm.quantized_mm(x[i:i + 1], wq, s, b) for i in range(M)])
+        assert torch.equal(full, singles)
+
+
+def test_empty_and_zero_inputs(vm, orc, cuda):
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, 64, 256, 64, 4, 5)
+    y = vm.quantized_mm(torch.empty(0, 256, device=cuda, dtype=torch.bfloat16), wq, s, b)
+    assert y.shape == (0, 64)
+    y = vm.quantized_mm(torch.zeros(2, 256, device=cuda, dtype=torch.bfloat16), wq, s, b)
+    assert torch.count_nonzero(y) == 0
+
+
+@pytest.mark.parametrize("sorted_indices", [False, True])
+@pytest.mark.parametrize("M", [1, 2])
+def test_gather_qmm(vm, orc, cuda, sorted_indices, M):
+    E, N, K, nb = 8, 96, 512, 24
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 51, lead=(E,))
+    rng = np.random.default_rng(52)
+    rhs = rng.integers(0, E, nb).astype(np.uint32)
+    rhs[3] = 5
+    if sorted_indices:
+        rhs = np.sort(rhs)
+    lhs = rng.integers(0, 6, nb).astype(np.uint32)
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (6, M, K)).astype(np.float32))
+    y = vm.gather_quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b,
+                               lhs_indices=torch.from_numpy(lhs.astype(np.int64)).to(cuda),
+                               rhs_indices=torch.from_numpy(rhs.astype(np.int64)).to(cuda),
+                               sorted_indices=sorted_indices)
+    ref = orc.gather_qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), lhs, rhs)
+    assert y.shape == (nb, M, N)
+    check_close(y.float().cpu().numpy(), ref)
+
+
+def test_gather_qmm_out_of_range_expert_gives_zeros(vm, orc, cuda):
+    E, N, K = 4, 32, 256
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 61, lead=(E,))
+    x = torch.randn(3, 1, K, device=cuda).bfloat16()
+    y = vm.gather_quantized_mm(x, wq, s, b, rhs_indices=torch.tensor([0, 9, 3], device=cuda))
+    assert torch.count_nonzero(y[1]) == 0 and torch.count_nonzero(y[0]) > 0
+
+
+@pytest.mark.parametrize("T", [1, 32, 256])
+def test_switch_glu_qwen3_moe_shape(vm, orc, cuda, T):
+    """hidden 2048, 128 experts, FFN 768, top-8 (reduced to
+    32 experts to keep the fp64 oracle fast; routing from softmax of N(0,1) fp32 logits)."""
+    E, D, F, k = 32, 2048, 768, 8
+    _, gate = make_weights(orc, vm, cuda, F, D, 64, 4, 71, lead=(E,))
+    _, up = make_weights(orc, vm, cuda, F, D, 64, 4, 72, lead=(E,))
+    _, down = make_weights(orc, vm, cuda, D, F, 64, 4, 73, lead=(E,))
+    rng = np.random.default_rng(74)
+    logits = rng.normal(0, 1, (T, E)).astype(np.float32)
+    inds, _ = orc.moe_route(logits, k)
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (T, D)).astype(np.float32))
+    glu = vm.SwitchGLU(vm.QuantizedSwitchLinear(*gate), vm.QuantizedSwitchLinear(*up),
+                       vm.QuantizedSwitchLinear(*down))
+    y = glu(to_dev_bf16(orc, xb, cuda), torch.from_numpy(inds.astype(np.int64)).to(cuda))
+    hostw = lambda t: (u32(t[0]), bits_of(t[1]), bits_of(t[2]))  # noqa: E731
+    ref = orc.switch_glu(xb, hostw(gate), hostw(up), hostw(down), inds)
+    assert y.shape == (T, k, D)
+    check_close(y.float().cpu().numpy(), ref)

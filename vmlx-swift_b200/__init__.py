@@ -1,0 +1,12 @@
+"""vmlx-swift_b200: B200-native (sm_100a) affine-quantized linear decode path.
+
+Host-side mirror of vmlx-swift's QuantizedLinear / SwitchGLU / MLXDistributedTP
+layers over the C ABI in include/vmlx_cuda.h (libvmlx_cuda.so, built in-tree).
+The directory name contains a hyphen, so load it with ``load_package()`` from
+the repository root helpers or importlib under the module name ``vmlx_b200``.
+"""
+from ._lib import VMLXError, build, lib  # noqa: F401
+from . import ops, nn, switch_layers  # noqa: F401
+from .ops import dequantized, gather_quantized_mm, quantized, quantized_mm  # noqa: F401
+from .nn import QuantizedLinear  # noqa: F401
+from .switch_layers import QuantizedSwitchLinear, SwitchGLU, gather_sort, scatter_unsort  # noqa: F401

@@ -1,0 +1,26 @@
+// api.cu -- error reporting and version of the C ABI.
+#include <string>
+
+#include "common.cuh"
+
+namespace vmlx {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+}  // namespace vmlx
+
+extern "C" const char* vmlx_last_error(void) { return vmlx::g_last_error.c_str(); }
+
+extern "C" int vmlx_version(void) { return 100; }

@@ -1,0 +1,72 @@
+// matmul.cu -- C-ABI entry points quantized_matmul / gather_qmm and their dispatch.
+#include "kernels.cuh"
+
+namespace vmlx {
+
+static int check_mm_args(const void* y, const void* x, const void* w, const void* s, const void* b,
+                         bool transpose, int gs, int bits, const char* mode, int64_t M, int64_t N,
+                         int64_t K) {
+  if (!mode_is_affine(mode)) return set_error(VMLX_E_UNSUPPORTED, "mode '%s' not supported", mode ? mode : "");
+  if (!transpose) return set_error(VMLX_E_UNSUPPORTED, "transpose=false is not supported");
+  if (bits != 4 && bits != 8) return set_error(VMLX_E_UNSUPPORTED, "bits=%d not supported for matmul (4, 8)", bits);
+  if (gs != 32 && gs != 64 && gs != 128) return set_error(VMLX_E_UNSUPPORTED, "group_size=%d not supported", gs);
+  if (!y || !x || !w || !s) return set_error(VMLX_E_INVALID, "null pointer");
+  if (!b) return set_error(VMLX_E_INVALID, "affine mode requires biases");
+  if (M < 0 || N <= 0 || K <= 0 || K % gs)
+    return set_error(VMLX_E_INVALID, "bad shape M=%lld N=%lld K=%lld (K must be a multiple of %d)",
+                     (long long)M, (long long)N, (long long)K, gs);
+  if (!aligned(x, 16) || !aligned(w, 16))
+    return set_error(VMLX_E_INVALID, "x and w must be 16-byte aligned");
+  return VMLX_OK;
+}
+
+static int nt_for(int64_t m) {
+  int64_t t = (m + 7) / 8;
+  return (int)(t < 1 ? 1 : (t > 4 ? 4 : t));
+}
+
+}  // namespace vmlx
+
+using namespace vmlx;
+
+extern "C" int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t* w, const void* scales,
+                                          const void* biases, bool transpose, int group_size, int bits,
+                                          const char* mode, int64_t M, int64_t N, int64_t K,
+                                          void* stream) {
+  int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
+  if (rc) return rc;
+  if (M == 0) return VMLX_OK;
+  cudaStream_t st = as_stream(stream);
+  if (M > 32) {
+    bool handled = false;
+    rc = launch_qmm_tc((const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, M, N, K,
+                       bits, group_size, st, &handled);
+    if (rc || handled) return rc;
+  }
+  QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
+            M, N, K, 0, 1, 1};
+  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, nt_for(M), st);
+}
+
+extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, const void* scales,
+                                    const void* biases, const uint32_t* lhs_indices,
+                                    const uint32_t* rhs_indices, bool transpose, int group_size,
+                                    int bits, const char* mode, bool sorted_indices, int64_t batch,
+                                    int64_t x_batches, int64_t M, int64_t N, int64_t K,
+                                    int64_t n_experts, void* stream) {
+  int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
+  if (rc) return rc;
+  if (!rhs_indices) return set_error(VMLX_E_INVALID, "rhs_indices is required");
+  if (batch < 0 || x_batches <= 0 || n_experts <= 0)
+    return set_error(VMLX_E_INVALID, "bad batch=%lld x_batches=%lld n_experts=%lld", (long long)batch,
+                     (long long)x_batches, (long long)n_experts);
+  if (!lhs_indices && batch % x_batches)
+    return set_error(VMLX_E_INVALID, "without lhs_indices, batch=%lld must be a multiple of x_batches=%lld",
+                     (long long)batch, (long long)x_batches);
+  if (batch == 0 || M == 0) return VMLX_OK;
+  QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, lhs_indices,
+            rhs_indices, M, N, K, batch, x_batches, n_experts};
+  cudaStream_t st = as_stream(stream);
+  if (sorted_indices) return launch_qmv(a, QMV_SORTED, bits, group_size, n_experts, 4, st);
+  return launch_qmv(a, QMV_GATHER, bits, group_size, batch, nt_for(M), st);
+}

@@ -1,0 +1,163 @@
+"""Array ops of the quantized path, mirroring MLX's Swift/C API.
+
+Names, argument meaning and defaults follow the reference:
+  quantized          Source/MLX/Ops.swift:2368-2388   (mlx_quantize)
+  dequantized        Source/MLX/Ops.swift:1146-1164   (mlx_dequantize)
+  quantized_mm       Source/MLX/Ops.swift:2427-2448   (mlx_quantized_matmul)
+  gather_quantized_mm Source/MLX/Ops.swift:1483-1505  (mlx_gather_qmm)
+Tensors are torch CUDA tensors (device memory and streams only); all compute
+runs in libvmlx_cuda.so on the caller's current CUDA stream.  Errors raised
+by the library surface as VMLXError, the analogue of MLX's error handler
+(Source/MLX/ErrorHandler.swift:52-121).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import VMLX_BF16, VMLX_F32, VMLXError, check
+
+__all__ = [
+    "quantized", "dequantized", "quantized_mm", "gather_quantized_mm", "VMLXError",
+    "pack_factor",
+]
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise VMLXError(_lib.VMLX_E_INVALID, "tensors must live on a CUDA device")
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return VMLX_BF16
+    if dt == torch.float32:
+        return VMLX_F32
+    raise VMLXError(_lib.VMLX_E_UNSUPPORTED, f"dtype {dt} not supported (bfloat16, float32)")
+
+
+def pack_factor(bits: int) -> int:
+    return 32 // bits
+
+
+def _consecutive_broadcast(xb_shape, bshape) -> bool:
+    """True when broadcasting x batches ``xb_shape`` to ``bshape`` maps flat
+    batch b to x batch b*x_batches/nb: x's batch dims (right-aligned) equal
+    bshape's leading dims and are 1 from the first difference on."""
+    xb = (1,) * (len(bshape) - len(xb_shape)) + tuple(xb_shape)
+    j = 0
+    while j < len(xb) and xb[j] == bshape[j]:
+        j += 1
+    return all(d == 1 for d in xb[j:])
+
+
+def quantized(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"
+              ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Quantize ``w [..., K]`` -> (wq uint32 [..., K*bits/32], scales, biases [..., K/g]).
+
+    scales/biases take w's dtype (bf16 or f32), as MLX does.  uint32 words are
+    returned as a torch.int32 tensor holding the same bits (torch has no uint32
+    arithmetic; the bit pattern is what matters)."""
+    _need_cuda(w)
+    w = w.contiguous()
+    K = w.shape[-1]
+    rows = w.numel() // K if K else 0
+    if K % group_size or (K * bits) % 32:
+        raise VMLXError(_lib.VMLX_E_INVALID, f"last dim {K} must be a multiple of group_size {group_size}")
+    wq = torch.empty(*w.shape[:-1], K * bits // 32, dtype=torch.int32, device=w.device)
+    scales = torch.empty(*w.shape[:-1], K // group_size, dtype=w.dtype, device=w.device)
+    biases = torch.empty_like(scales)
+    check(_lib.lib().vmlx_cuda_quantize(
+        wq.data_ptr(), scales.data_ptr(), biases.data_ptr(), w.data_ptr(), _dtype_code(w.dtype),
+        rows, K, group_size, bits, mode.encode() if mode else None, _stream(w)))
+    return wq, scales, biases
+
+
+def dequantized(wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64,
+                bits: int = 4, mode: str = "affine", dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """w = scale*q + bias (fp32 math), returned in ``dtype`` (default: scales' dtype)."""
+    _need_cuda(wq, scales, biases)
+    dtype = dtype or scales.dtype
+    K = wq.shape[-1] * 32 // bits
+    rows = wq.numel() // wq.shape[-1]
+    out = torch.empty(*wq.shape[:-1], K, dtype=dtype, device=wq.device)
+    check(_lib.lib().vmlx_cuda_dequantize(
+        out.data_ptr(), _dtype_code(dtype), wq.contiguous().data_ptr(), scales.contiguous().data_ptr(),
+        biases.contiguous().data_ptr(), _dtype_code(scales.dtype), rows, K, group_size, bits,
+        mode.encode() if mode else None, _stream(wq)))
+    return out
+
+
+def quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
+                 transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x [..., K] @ dequantized(w [N, K*bits/32])^T`` in bf16 (fp32 accumulation)."""
+    _need_cuda(x, w, scales, biases)
+    if x.dtype != torch.bfloat16:
+        raise VMLXError(_lib.VMLX_E_UNSUPPORTED, "quantized_mm: x must be bfloat16")
+    x = x.contiguous()
+    K = x.shape[-1]
+    N = w.shape[-2]
+    M = x.numel() // K if K else 0
+    if w.shape[-1] * 32 // bits != K:
+        raise VMLXError(_lib.VMLX_E_INVALID, f"x K={K} does not match w K={w.shape[-1] * 32 // bits}")
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    check(_lib.lib().vmlx_cuda_quantized_matmul(
+        out.data_ptr(), x.data_ptr(), w.data_ptr(), scales.data_ptr(),
+        biases.data_ptr() if biases is not None else None, transpose, group_size, bits,
+        mode.encode() if mode else None, M, N, K, _stream(x)))
+    return out
+
+
+def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                        biases: Optional[torch.Tensor], lhs_indices: Optional[torch.Tensor] = None,
+                        rhs_indices: Optional[torch.Tensor] = None, transpose: bool = True,
+                        group_size: int = 64, bits: int = 4, mode: str = "affine",
+                        sorted_indices: bool = False) -> torch.Tensor:
+    """MLX gather_qmm: ``y[i] = x[lhs[i]] @ dequantized(w[rhs[i]])^T`` with broadcasting.
+
+    x [*xb, M, K]; w [E, N, K*bits/32]; indices int tensors.  The output shape
+    is broadcast(index shapes, xb) + [M, N], as in MLX."""
+    _need_cuda(x, w, scales, biases, lhs_indices, rhs_indices)
+    if x.dtype != torch.bfloat16:
+        raise VMLXError(_lib.VMLX_E_UNSUPPORTED, "gather_quantized_mm: x must be bfloat16")
+    if rhs_indices is None:
+        raise VMLXError(_lib.VMLX_E_INVALID, "rhs_indices is required for a stacked weight")
+    x = x.contiguous()
+    M, K = x.shape[-2], x.shape[-1]
+    xb_shape = tuple(x.shape[:-2])
+    E, N = w.shape[0], w.shape[-2]
+    x_batches = 1
+    for d in xb_shape:
+        x_batches *= d
+    if lhs_indices is None:
+        bshape = torch.broadcast_shapes(xb_shape, tuple(rhs_indices.shape))
+        rhs = rhs_indices.expand(bshape).reshape(-1)
+        nb = rhs.numel()
+        # x batch broadcast: use the implicit "consecutive" rule when it is
+        # exact, else materialise lhs as the broadcast of arange(x batches).
+        lhs = None if _consecutive_broadcast(xb_shape, bshape) else (
+            torch.arange(x_batches, device=x.device, dtype=torch.int64)
+            .reshape(xb_shape or (1,)).expand(bshape).reshape(-1))
+    else:
+        bshape = torch.broadcast_shapes(tuple(lhs_indices.shape), tuple(rhs_indices.shape))
+        rhs = rhs_indices.expand(bshape).reshape(-1)
+        lhs = lhs_indices.expand(bshape).reshape(-1)
+    rhs32 = rhs.to(torch.int32).contiguous()
+    lhs32 = lhs.to(torch.int32).contiguous() if lhs is not None else None
+    nb = rhs32.numel()
+    y = torch.empty(*bshape, M, N, dtype=torch.bfloat16, device=x.device)
+    check(_lib.lib().vmlx_cuda_gather_qmm(
+        y.data_ptr(), x.data_ptr(), w.data_ptr(), scales.data_ptr(),
+        biases.data_ptr() if biases is not None else None,
+        lhs32.data_ptr() if lhs32 is not None else None, rhs32.data_ptr(), transpose, group_size,
+        bits, mode.encode() if mode else None, sorted_indices, nb, x_batches, M, N, K, E, _stream(x)))
+    return y
