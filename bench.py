@@ -129,15 +129,16 @@ def time_graph_calls(torch, fn_list, reps, warmup, stream):
         with torch.cuda.graph(g, stream=stream):
             for f in fn_list:
                 f()
-    for _ in range(warmup):
-        g.replay()
-    torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        g.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        for _ in range(warmup):
+            g.replay()
+        stream.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / 1e3 / (reps * len(fn_list))
 

@@ -72,8 +72,8 @@ VMLX_API int vmlx_cuda_quantize(void* wq, void* scales, void* biases, const void
                        void* stream);
 
 /*
- * Affine dequantization: out[r, k] = scale*q + bias, computed in fp32 and
- * stored as out_dtype (VMLX_F32: exact; VMLX_BF16: round to nearest even).
+ * Affine dequantization: out[r, k] = scale*q + bias, computed in fp32 as an
+ * unfused multiply then add (exact product for bf16 scales) and stored as out_dtype (VMLX_F32: exact; VMLX_BF16: round to nearest even).
  * Replaces mlx_dequantize (Source/Cmlx/include/mlx/c/ops.h:359-369);
  * arithmetic of affine_dequantize (quantized.h:2498-2558).
  * scales_dtype gives the dtype of scales/biases.

@@ -154,7 +154,9 @@ static inline uint32_t code_at(const uint32_t* row, int64_t k, int bits) {
 }
 
 /* Dequantize (quantized.h:2498-2558): out = float(scale)*q + float(bias),
- * computed in fp32 (the product is exact, so fma and mul+add agree).
+ * computed in fp32 as an unfused multiply then add (built with
+ * -ffp-contract=off); for bf16 scales the product is exact, so this also equals
+ * the fused form.
  * scales_bf16 != 0 means scales/biases are bf16 bit patterns, else f32. */
 int vq_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scales_bf16,
                   int64_t rows, int64_t cols, int gs, int bits, float* out) {

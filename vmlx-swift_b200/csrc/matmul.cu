@@ -33,9 +33,9 @@ extern "C" int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t
                                           const void* biases, bool transpose, int group_size, int bits,
                                           const char* mode, int64_t M, int64_t N, int64_t K,
                                           void* stream) {
+  if (M == 0 && N > 0 && K > 0) return VMLX_OK;  // empty input: nothing to read or write
   int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
   if (rc) return rc;
-  if (M == 0) return VMLX_OK;
   cudaStream_t st = as_stream(stream);
   if (M > 32) {
     bool handled = false;

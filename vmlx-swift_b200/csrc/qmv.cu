@@ -11,10 +11,13 @@
 // MMA) and its 8 warps split K into contiguous ranges.  Per group of g weights
 // every lane streams g*bits/128 words of two rows (row r and r+8) with
 // L1-bypassing vector loads -- the four lanes of a quad cover one group of one
-// row, i.e. whole 32-byte sectors -- dequantizes them in registers straight
-// into bf16 A fragments (4-bit: prmt with a 0x43 exponent byte gives 128+q
-// exactly, then one sub and one fma per pair; 8-bit: the 2^23 float trick),
-// and issues mma.m16n8k16 (bf16 in, fp32 accumulate) against x in B fragments.
+// row, i.e. whole 32-byte sectors -- and unpacks the codes in registers into
+// bf16 A fragments holding q exactly (4-bit: prmt with a 0x43 exponent byte
+// gives 128+q; 8-bit: the 2^23 float trick).  mma.m16n8k16 (bf16 in, fp32
+// accumulate) forms sum(x*q) per group with exact products, a second MMA
+// against an all-ones tile forms sum(x), and the group is folded as
+// scale*sum(x*q) + bias*sum(x) -- the factorisation of MLX's qdot
+// (quantized.h:209-316), so no rounded bf16 weight is ever formed.
 // Because a dot product does not care about the order of k, the nibbles are
 // used in the order the unpack produces them and x is permuted to match
 // (four prmt per eight x values), so no shifts by position are needed.
@@ -68,51 +71,29 @@ __device__ __forceinline__ void token_rows(const QmvArgs& p, int mode, int64_t b
   }
 }
 
-// Dequantize one 4-bit word of each of the two rows into the A fragments of
-// its two k16 steps.  a[0] = step using nibbles (0,2 | 4,6), a[1] = (1,3 | 5,7).
-__device__ __forceinline__ void deq4_word(uint32_t w0, uint32_t w1, bf162 s0, bf162 b0, bf162 s1,
-                                          bf162 b1, uint32_t (&a)[2][4]) {
+// Unpack one 4-bit word into bf16 pairs holding 128+q exactly (prmt with a
+// 0x43 exponent byte).  p[0] = nibbles (0,2), p[1] = (4,6), p[2] = (1,3),
+// p[3] = (5,7): the order the two masks produce, matched by the x permutation.
+__device__ __forceinline__ void unpack4(uint32_t w, uint32_t (&p)[4]) {
   const uint32_t C43 = 0x43434343u;
-  const bf162 k128 = u32_as_bf162(0x43004300u);
-  uint32_t lo0 = w0 & 0x0F0F0F0Fu, hi0 = (w0 >> 4) & 0x0F0F0F0Fu;
-  uint32_t lo1 = w1 & 0x0F0F0F0Fu, hi1 = (w1 >> 4) & 0x0F0F0F0Fu;
-  uint32_t p[2][4];
-  p[0][0] = prmt(lo0, C43, 0x4140);
-  p[0][1] = prmt(lo0, C43, 0x4342);
-  p[0][2] = prmt(hi0, C43, 0x4140);
-  p[0][3] = prmt(hi0, C43, 0x4342);
-  p[1][0] = prmt(lo1, C43, 0x4140);
-  p[1][1] = prmt(lo1, C43, 0x4342);
-  p[1][2] = prmt(hi1, C43, 0x4140);
-  p[1][3] = prmt(hi1, C43, 0x4342);
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    p[0][i] = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(p[0][i]), k128), s0, b0));
-    p[1][i] = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(p[1][i]), k128), s1, b1));
-  }
-  // A fragment registers: {row g k-lo, row g+8 k-lo, row g k-hi, row g+8 k-hi}
-  a[0][0] = p[0][0]; a[0][1] = p[1][0]; a[0][2] = p[0][1]; a[0][3] = p[1][1];
-  a[1][0] = p[0][2]; a[1][1] = p[1][2]; a[1][2] = p[0][3]; a[1][3] = p[1][3];
+  uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+  p[0] = prmt(lo, C43, 0x4140);
+  p[1] = prmt(lo, C43, 0x4342);
+  p[2] = prmt(hi, C43, 0x4140);
+  p[3] = prmt(hi, C43, 0x4342);
 }
 
-// Dequantize one 8-bit word (4 consecutive k) of each row into one k16 step.
-__device__ __forceinline__ void deq8_word(uint32_t w0, uint32_t w1, bf162 s0, bf162 b0, bf162 s1,
-                                          bf162 b1, uint32_t (&a)[4]) {
+// Unpack one 8-bit word (4 consecutive k) into two bf16 pairs holding q exactly
+// (the 2^23 float trick, then a packed convert; q <= 255 is exact in bf16).
+__device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&p)[2]) {
   const float MAGIC = 8388608.0f;
   const uint32_t K4B = 0x4B000000u;
-  float f0[4], f1[4];
-  f0[0] = __uint_as_float(prmt(w0, K4B, 0x7540)) - MAGIC;
-  f0[1] = __uint_as_float(prmt(w0, K4B, 0x7541)) - MAGIC;
-  f0[2] = __uint_as_float(prmt(w0, K4B, 0x7542)) - MAGIC;
-  f0[3] = __uint_as_float(prmt(w0, K4B, 0x7543)) - MAGIC;
-  f1[0] = __uint_as_float(prmt(w1, K4B, 0x7540)) - MAGIC;
-  f1[1] = __uint_as_float(prmt(w1, K4B, 0x7541)) - MAGIC;
-  f1[2] = __uint_as_float(prmt(w1, K4B, 0x7542)) - MAGIC;
-  f1[3] = __uint_as_float(prmt(w1, K4B, 0x7543)) - MAGIC;
-  a[0] = bf162_as_u32(__hfma2(__floats2bfloat162_rn(f0[0], f0[1]), s0, b0));
-  a[1] = bf162_as_u32(__hfma2(__floats2bfloat162_rn(f1[0], f1[1]), s1, b1));
-  a[2] = bf162_as_u32(__hfma2(__floats2bfloat162_rn(f0[2], f0[3]), s0, b0));
-  a[3] = bf162_as_u32(__hfma2(__floats2bfloat162_rn(f1[2], f1[3]), s1, b1));
+  float f0 = __uint_as_float(prmt(w, K4B, 0x7540)) - MAGIC;
+  float f1 = __uint_as_float(prmt(w, K4B, 0x7541)) - MAGIC;
+  float f2 = __uint_as_float(prmt(w, K4B, 0x7542)) - MAGIC;
+  float f3 = __uint_as_float(prmt(w, K4B, 0x7543)) - MAGIC;
+  p[0] = bf162_as_u32(__floats2bfloat162_rn(f0, f1));
+  p[1] = bf162_as_u32(__floats2bfloat162_rn(f2, f3));
 }
 
 template <int BITS, int GS, int NT>
@@ -122,6 +103,8 @@ qmv_kernel(QmvArgs p, int mode) {
   constexpr int WPL = T::WPL, VPL = T::VPL, WPG = T::WPG, U = T::U;
   __shared__ float red[QMV_WARPS][NT * 8][QMV_ROWS + 1];
 
+  // A fragment of an all-ones 16x16 bf16 tile (1.0 = 0x3F80)
+  const uint32_t kOnes[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, c = lane & 3;
   const int64_t n0 = (int64_t)blockIdx.x * QMV_ROWS;
@@ -189,7 +172,7 @@ qmv_kernel(QmvArgs p, int mode) {
     if (!zero_rows) {
       for (int64_t g = g0; g < g1; g += U) {
         uint32_t wv0[U][WPL], wv1[U][WPL];
-        bf162 sv0[U], bv0[U], sv1[U], bv1[U];
+        bf16 sv0[U], bv0[U], sv1[U], bv1[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
           if (g + u < g1) {
@@ -211,21 +194,32 @@ qmv_kernel(QmvArgs p, int mode) {
                 wv1[u][q] = a1.x; wv1[u][q + 1] = a1.y; wv1[u][q + 2] = a1.z; wv1[u][q + 3] = a1.w;
               }
             }
-            sv0[u] = __bfloat162bfloat162(s0p[gg]);
-            bv0[u] = __bfloat162bfloat162(b0p[gg]);
-            sv1[u] = __bfloat162bfloat162(s1p[gg]);
-            bv1[u] = __bfloat162bfloat162(b1p[gg]);
+            sv0[u] = s0p[gg];
+            bv0[u] = b0p[gg];
+            sv1[u] = s1p[gg];
+            bv1[u] = b1p[gg];
           }
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
           if (g + u < g1) {
             const int64_t kbase = (g + u) * GS + c * VPL;
+            // Per group: ag = sum_k x*code (exact products, fp32 accumulate),
+            // xg = sum_k x (an MMA against an all-ones A tile), then
+            // y += scale*ag + bias*xg as MLX's qdot does (quantized.h:209-316).
+            float ag[NT][4], xg[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+              for (int i = 0; i < 4; i++) ag[t][i] = xg[t][i] = 0.f;
 #pragma unroll
             for (int wi = 0; wi < WPL; wi++) {
               if constexpr (BITS == 4) {
-                uint32_t a[2][4];
-                deq4_word(wv0[u][wi], wv1[u][wi], sv0[u], bv0[u], sv1[u], bv1[u], a);
+                uint32_t p0[4], p1[4];
+                unpack4(wv0[u][wi], p0);
+                unpack4(wv1[u][wi], p1);
+                const uint32_t a0[4] = {p0[0], p1[0], p0[1], p1[1]};
+                const uint32_t a1[4] = {p0[2], p1[2], p0[3], p1[3]};
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                   uint32_t x02 = 0, x46 = 0, x13 = 0, x57 = 0;
@@ -236,12 +230,16 @@ qmv_kernel(QmvArgs p, int mode) {
                     x13 = prmt(xv.x, xv.y, 0x7632);
                     x57 = prmt(xv.z, xv.w, 0x7632);
                   }
-                  mma_bf16_16816(acc[t], a[0], x02, x46);
-                  mma_bf16_16816(acc[t], a[1], x13, x57);
+                  mma_bf16_16816(ag[t], a0, x02, x46);
+                  mma_bf16_16816(ag[t], a1, x13, x57);
+                  mma_bf16_16816(xg[t], kOnes, x02, x46);
+                  mma_bf16_16816(xg[t], kOnes, x13, x57);
                 }
               } else {
-                uint32_t a[4];
-                deq8_word(wv0[u][wi], wv1[u][wi], sv0[u], bv0[u], sv1[u], bv1[u], a);
+                uint32_t p0[2], p1[2];
+                unpack8(wv0[u][wi], p0);
+                unpack8(wv1[u][wi], p1);
+                const uint32_t a[4] = {p0[0], p1[0], p0[1], p1[1]};
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                   uint32_t x01 = 0, x23 = 0;
@@ -250,9 +248,21 @@ qmv_kernel(QmvArgs p, int mode) {
                     x01 = xv.x;
                     x23 = xv.y;
                   }
-                  mma_bf16_16816(acc[t], a, x01, x23);
+                  mma_bf16_16816(ag[t], a, x01, x23);
+                  mma_bf16_16816(xg[t], kOnes, x01, x23);
                 }
               }
+            }
+            const float s0 = __bfloat162float(sv0[u]), s1 = __bfloat162float(sv1[u]);
+            // 4-bit codes carry +128: fold -128*scale*sum(x) into the bias term
+            const float c0 = BITS == 4 ? fmaf(-128.f, s0, __bfloat162float(bv0[u])) : __bfloat162float(bv0[u]);
+            const float c1 = BITS == 4 ? fmaf(-128.f, s1, __bfloat162float(bv1[u])) : __bfloat162float(bv1[u]);
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+              acc[t][0] = fmaf(s0, ag[t][0], fmaf(c0, xg[t][0], acc[t][0]));
+              acc[t][1] = fmaf(s0, ag[t][1], fmaf(c0, xg[t][1], acc[t][1]));
+              acc[t][2] = fmaf(s1, ag[t][2], fmaf(c1, xg[t][2], acc[t][2]));
+              acc[t][3] = fmaf(s1, ag[t][3], fmaf(c1, xg[t][3], acc[t][3]));
             }
           }
         }

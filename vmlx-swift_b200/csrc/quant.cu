@@ -5,9 +5,10 @@
 // min/max/edge rule, IEEE division, round-half-away-from-zero (roundf) and
 // LSB-first packing.  This file must not be built with fast-math.
 //
-// Layout: one warp per (row, run of 32 groups); lane i owns group i of the run,
-// reads it with 16-byte loads and writes its packed words.  Quantization runs
-// at load time only, so the kernel is simple rather than bandwidth-tuned.
+// Layout: one thread per group (groups are contiguous in a row-major matrix);
+// it reads its g values, derives scale/bias and writes g*bits/32 packed words.
+// Quantization runs at load time only, so the kernel is simple rather than
+// bandwidth-tuned.
 #include "common.cuh"
 
 namespace vmlx {
@@ -104,7 +105,7 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const TS* __r
 #pragma unroll
   for (int j = 0; j < PER; j++) {
     float q = (float)((word >> (BITS * j)) & ((1u << BITS) - 1u));
-    out[k0 + j] = from_f32<TO>(__fmaf_rn(s, q, b));  // s*q is exact: fma == mul+add
+    out[k0 + j] = from_f32<TO>(__fadd_rn(__fmul_rn(s, q), b));  // unfused, as written in the source
   }
 }
 
