@@ -23,9 +23,10 @@ struct QmvArgs {
   int64_t batch;      // gather: number of batch elements
   int64_t x_batches;  // gather: number of x matrices
   int64_t n_experts;
+  int* status;  // optional device word set to VMLX_E_STATE if a bounded wait ran out
 };
 
-int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t grid_y, int nt, cudaStream_t st);
+int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int toka, cudaStream_t st);
 
 // tcgen05 GEMM for M > 32; sets *handled = false when the shape is not covered.
 int launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y,

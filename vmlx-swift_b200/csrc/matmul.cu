@@ -20,10 +20,7 @@ static int check_mm_args(const void* y, const void* x, const void* w, const void
   return VMLX_OK;
 }
 
-static int nt_for(int64_t m) {
-  int64_t t = (m + 7) / 8;
-  return (int)(t < 1 ? 1 : (t > 4 ? 4 : t));
-}
+static int toka_for(int64_t m) { return (int)(m < 1 ? 1 : (m > 32 ? 32 : m)); }
 
 }  // namespace vmlx
 
@@ -45,7 +42,7 @@ extern "C" int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t
   }
   QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
             M, N, K, 0, 1, 1};
-  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, nt_for(M), st);
+  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, toka_for(M), st);
 }
 
 extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, const void* scales,
@@ -67,6 +64,11 @@ extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, c
   QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, lhs_indices,
             rhs_indices, M, N, K, batch, x_batches, n_experts};
   cudaStream_t st = as_stream(stream);
-  if (sorted_indices) return launch_qmv(a, QMV_SORTED, bits, group_size, n_experts, 4, st);
-  return launch_qmv(a, QMV_GATHER, bits, group_size, batch, nt_for(M), st);
+  if (sorted_indices) {
+    // rows per expert on average, staged in passes of up to 32 rows
+    int64_t avg = (batch * M + n_experts - 1) / n_experts;
+    int toka = (int)((avg + avg / 2 + 7) / 8 * 8);
+    return launch_qmv(a, QMV_SORTED, bits, group_size, n_experts, toka, st);
+  }
+  return launch_qmv(a, QMV_GATHER, bits, group_size, batch, toka_for(M), st);
 }

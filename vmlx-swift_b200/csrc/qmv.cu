@@ -6,39 +6,51 @@
 // variants affine_gather_qmv(_fast) (:1875-1997) / sorted affine_gather_qmm_rhs
 // (:2197-2391) for small runs.
 //
-// B200 design.  The op is HBM-bound: 0.5625 B/weight (4-bit, g64, bf16
-// scale+bias).  Each CTA owns 16 output rows (one m16 tile of the tensor-core
-// MMA) and its 8 warps split K into contiguous ranges.  Per group of g weights
-// every lane streams g*bits/128 words of two rows (row r and r+8) with
-// L1-bypassing vector loads -- the four lanes of a quad cover one group of one
-// row, i.e. whole 32-byte sectors -- and unpacks the codes in registers into
-// bf16 A fragments holding q exactly (4-bit: prmt with a 0x43 exponent byte
-// gives 128+q; 8-bit: the 2^23 float trick).  mma.m16n8k16 (bf16 in, fp32
-// accumulate) forms sum(x*q) per group with exact products, a second MMA
-// against an all-ones tile forms sum(x), and the group is folded as
-// scale*sum(x*q) + bias*sum(x) -- the factorisation of MLX's qdot
-// (quantized.h:209-316), so no rounded bf16 weight is ever formed.
-// Because a dot product does not care about the order of k, the nibbles are
-// used in the order the unpack produces them and x is permuted to match
-// (four prmt per eight x values), so no shifts by position are needed.
-// Tokens are the MMA's N dimension (8 per tile, up to 4 tiles = 32 rows).
-// The 8 warps' partial tiles are summed through shared memory and written
-// once as bf16: no global scratch, no atomics, deterministic, and each row's
-// result does not depend on M (batch invariance, as the reference's
-// QuantizedSmallMScalingBenchTests.swift:110-127 requires).
+// B200 design.  The op is HBM-bound (0.5625 B/weight at 4-bit g64 with bf16
+// scale+bias), so the kernel is built to keep HBM busy:
+//  * Persistent CTAs.  A work item is a tile of 64 output rows (x one expert
+//    in the gathered modes).  The K range is split over a thread-block
+//    cluster of C CTAs (1..8) whose partial tiles are added through
+//    distributed shared memory: no global scratch, no atomics.
+//  * Warp 4 is the producer: one TMA instruction (cp.async.bulk.tensor.2d,
+//    128-byte swizzle, no multicast) moves a 64-row x 128-byte stage of packed
+//    weights into a ring of shared-memory stages completing on mbarriers, and
+//    two more move the item's bf16 scales and biases.  It runs ahead across
+//    item boundaries, so HBM stays busy while consumers finish a tile.
+//  * Warps 0-3 are consumers, 16 rows each (one m16 tile of mma.m16n8k16).
+//    They unpack codes from shared memory into bf16 A fragments holding q
+//    exactly (4-bit: prmt with a 0x43 exponent byte gives 128+q; 8-bit: the
+//    2^23 float trick) and form sum(x*q) per group with exact products in
+//    fp32.  x was staged once per CTA in fragment order together with its
+//    per-group sums, so each group is folded as scale*sum(x*q) + bias*sum(x),
+//    the factorisation of MLX's qdot (quantized.h:209-316); no rounded bf16
+//    weight is ever formed.
+//  * A dot product does not care about the order of k: the nibbles are used
+//    in the order the unpack produces them and x is permuted to match.
+//  * Tokens are the MMA's N dimension (8 per tile, up to 4 tiles = 32 rows).
+// Each row's result does not depend on M (batch invariance, as the
+// reference's QuantizedSmallMScalingBenchTests.swift:110-127 requires).
 #include "kernels.cuh"
+#include "sm100_util.cuh"
+#include "tmap.cuh"
 
 namespace vmlx {
 
-constexpr int QMV_WARPS = 8;
-constexpr int QMV_ROWS = 16;
+namespace cg = cooperative_groups;
+
+constexpr int QMV_CWARPS = 4;                 // consumer warps
+constexpr int QMV_ROWS = 16 * QMV_CWARPS;     // rows per work item
+constexpr int QMV_THREADS = 32 * (QMV_CWARPS + 1);
+constexpr int QMV_STAGES = 6;
+constexpr int QMV_MAX_CLUSTER = 8;
 
 template <int BITS, int GS>
 struct QT {
-  static constexpr int WPL = GS * BITS / 128;  // words per lane per row per group
-  static constexpr int VPL = GS / 4;           // k values per lane per group
-  static constexpr int WPG = GS * BITS / 32;   // words per row per group
-  static constexpr int U = (16 / WPL) < 1 ? 1 : (16 / WPL);  // groups in flight per warp
+  static constexpr int WPL = GS * BITS / 128;   // words per lane per row per group
+  static constexpr int VPL = GS / 4;            // k values per lane per group
+  static constexpr int GB = GS * BITS / 8;      // bytes per row per group
+  static constexpr int SG = 128 / GB;           // groups per stage: one 128-byte swizzle span per row
+  static constexpr int FB = BITS == 4 ? 16 : 8; // x fragment bytes per lane per word
 };
 
 // Lower bound of `e` in the non-decreasing array a[0, n).
@@ -96,228 +108,480 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&p)[2]) {
   p[1] = bf162_as_u32(__floats2bfloat162_rn(f2, f3));
 }
 
-template <int BITS, int GS, int NT>
-__global__ void __launch_bounds__(QMV_WARPS * 32)
-qmv_kernel(QmvArgs p, int mode) {
-  using T = QT<BITS, GS>;
-  constexpr int WPL = T::WPL, VPL = T::VPL, WPG = T::WPG, U = T::U;
-  __shared__ float red[QMV_WARPS][NT * 8][QMV_ROWS + 1];
+// Shared-memory plan of one CTA; sizes depend on the K-slice (ks groups) and
+// on the number of token rows staged at once (tok).  The ring is 1024-byte
+// aligned (the 128-byte TMA swizzle atom).
+struct QmvPlan {
+  int ks, tok, ws, wpl, fb;
+  size_t o_ring, o_sc, o_bar, o_xfrag, o_xsum, o_red, total;
+  __host__ __device__ void init(int bits, int gs, int ks_, int tok_) {
+    ks = ks_;
+    tok = tok_;
+    ws = ((ks + 7) + 7) / 8 * 8;  // scale window (elements), 16-byte multiple
+    wpl = gs * bits / 128;
+    fb = bits == 4 ? 16 : 8;
+    o_ring = 0;
+    o_sc = o_ring + (size_t)QMV_STAGES * QMV_ROWS * 128;
+    o_bar = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
+    o_xfrag = o_bar + (2 * QMV_STAGES + 4) * sizeof(uint64_t);
+    o_xsum = o_xfrag + (size_t)ks * wpl * tok * 4 * fb;
+    o_red = o_xsum + (((size_t)ks * tok * 4 + 15) / 16) * 16;
+    total = o_red + (size_t)2 * QMV_ROWS * tok * 4 + 1024;  // + alignment slack
+  }
+};
 
-  // A fragment of an all-ones 16x16 bf16 tile (1.0 = 0x3F80)
-  const uint32_t kOnes[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gq = lane >> 2, c = lane & 3;
-  const int64_t n0 = (int64_t)blockIdx.x * QMV_ROWS;
-  const int64_t KG = p.K / GS;
-  const int64_t wrow = p.K * BITS / 32;  // words per weight row
+// Work item -> (row tile, z) and the token set / expert of z.
+struct QmvItem {
+  int64_t n0, base, ntok, e;  // e: expert (0 for dense)
+  bool zero_rows;
+};
 
-  // ---- which weight matrix and which tokens this CTA serves ----
-  const uint32_t* W = p.w;
-  const bf16* S = p.scales;
-  const bf16* B = p.biases;
-  int64_t ntok_total = p.M, base = 0;
-  bool zero_rows = false;
+__device__ __forceinline__ QmvItem qmv_item(const QmvArgs& p, int mode, int64_t item, int64_t rowtiles) {
+  QmvItem it;
+  const int64_t z = item / rowtiles;
+  it.n0 = (item - z * rowtiles) * QMV_ROWS;
+  it.base = 0;
+  it.ntok = p.M;
+  it.e = 0;
+  it.zero_rows = false;
   if (mode == QMV_GATHER) {
-    base = blockIdx.y;
-    uint32_t e = p.rhs[base];
-    if ((int64_t)e >= p.n_experts) zero_rows = true;
-    else {
-      W += (int64_t)e * p.N * wrow;
-      S += (int64_t)e * p.N * KG;
-      B += (int64_t)e * p.N * KG;
-    }
+    it.base = z;
+    it.e = (int64_t)p.rhs[z];
+    if (it.e >= p.n_experts) { it.zero_rows = true; it.e = 0; }
   } else if (mode == QMV_SORTED) {
-    uint32_t e = blockIdx.y;
-    int64_t lo = lower_bound_u32(p.rhs, p.batch, e);
-    int64_t hi = lower_bound_u32(p.rhs, p.batch, e + 1);
-    if (lo >= hi) return;  // no rows routed to this expert
-    base = lo * p.M;
-    ntok_total = (hi - lo) * p.M;
-    W += (int64_t)e * p.N * wrow;
-    S += (int64_t)e * p.N * KG;
-    B += (int64_t)e * p.N * KG;
+    it.e = z;
+    const int64_t lo = lower_bound_u32(p.rhs, p.batch, (uint32_t)z);
+    const int64_t hi = lower_bound_u32(p.rhs, p.batch, (uint32_t)z + 1);
+    it.base = lo * p.M;
+    it.ntok = (hi - lo) * p.M;
   }
+  return it;
+}
 
-  // rows owned by this lane (clamped for loads; results past N are dropped)
-  const int64_t r0 = n0 + gq, r1 = n0 + gq + 8;
-  const int64_t r0c = r0 < p.N ? r0 : p.N - 1, r1c = r1 < p.N ? r1 : p.N - 1;
-  const uint32_t* w0p = W + r0c * wrow + c * WPL;
-  const uint32_t* w1p = W + r1c * wrow + c * WPL;
-  const bf16* s0p = S + r0c * KG;
-  const bf16* s1p = S + r1c * KG;
-  const bf16* b0p = B + r0c * KG;
-  const bf16* b1p = B + r1c * KG;
+// Byte offset of (row, byte o) inside a 128B-swizzled [rows][128] TMA tile:
+// 16-byte chunk index XOR (row mod 8).
+__device__ __forceinline__ uint32_t swz128(int r, int o) {
+  return (uint32_t)(r * 128 + ((((o >> 4) ^ (r & 7))) << 4) + (o & 15));
+}
 
-  // contiguous K split over warps (in groups)
-  const int64_t gper = (KG + QMV_WARPS - 1) / QMV_WARPS;
-  const int64_t g0 = warp * gper;
-  const int64_t g1 = (g0 + gper < KG) ? g0 + gper : KG;
+template <int BITS, int GS, int NT>
+__global__ void __launch_bounds__(QMV_THREADS, 1)
+qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
+           const __grid_constant__ CUtensorMap tmb, int sc_tma, int mode, int Ks, int C, int TOKA,
+           int64_t rowtiles, int64_t n_items) {
+  using T = QT<BITS, GS>;
+  constexpr int WPL = T::WPL, VPL = T::VPL, GB = T::GB, SG = T::SG, FB = T::FB;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  QmvPlan L;
+  L.init(BITS, GS, Ks, TOKA);
+  const int WS = L.ws;
 
-  for (int64_t chunk = 0; chunk < ntok_total; chunk += NT * 8) {
-    const int64_t ntok = (ntok_total - chunk) < NT * 8 ? (ntok_total - chunk) : NT * 8;
-    // x row of this lane's B-fragment token in each tile
-    const bf16* xr[NT];
-#pragma unroll
-    for (int t = 0; t < NT; t++) {
-      int64_t tok = t * 8 + gq;
-      bf16* yr_unused;
-      xr[t] = nullptr;
-      if (tok < ntok && !zero_rows) token_rows(p, mode, base, chunk + tok, xr[t], yr_unused);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rank = (int)(blockIdx.x % C);  // K-slice == rank in the cluster (cluster dims (C,1,1))
+  const int64_t cluster_id = blockIdx.x / C, n_clusters = gridDim.x / C;
+  const int64_t KG = p.K / GS;
+  const int64_t gs0 = (int64_t)rank * Ks;
+  const int nG = (int)(gs0 >= KG ? 0 : (KG - gs0 < Ks ? KG - gs0 : Ks));
+  const int nst = (nG + SG - 1) / SG;
+  const int xs0 = (int)(gs0 & ~(int64_t)7);  // scale window start (16-byte aligned column)
+  const int soff = (int)(gs0 - xs0);
+
+  uint8_t* ring = smem + L.o_ring;
+  bf16* scb = reinterpret_cast<bf16*>(smem + L.o_sc);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.o_bar);
+  uint64_t* empty = full + QMV_STAGES;
+  uint64_t* scfull = empty + QMV_STAGES;
+  uint64_t* scempty = scfull + 2;
+  uint8_t* xfrag = smem + L.o_xfrag;
+  float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);
+  float* red = reinterpret_cast<float*>(smem + L.o_red);
+
+  if (tid == 0) {
+    for (int s = 0; s < QMV_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], QMV_CWARPS);
     }
+    for (int s = 0; s < 2; s++) {
+      mbar_init(&scfull[s], 1);
+      mbar_init(&scempty[s], QMV_CWARPS);
+    }
+    fence_mbar_init();
+  }
+  if (warp == QMV_CWARPS && lane == 0) {
+    tma_prefetch_desc(&tmw);
+    if (sc_tma) { tma_prefetch_desc(&tms); tma_prefetch_desc(&tmb); }
+  }
+  __syncthreads();
 
-    float acc[NT][4];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+  bool ok = true;
+  uint32_t it_stage = 0, ic = 0;
 
-    if (!zero_rows) {
-      for (int64_t g = g0; g < g1; g += U) {
-        uint32_t wv0[U][WPL], wv1[U][WPL];
-        bf16 sv0[U], bv0[U], sv1[U], bv1[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          if (g + u < g1) {
-            const int64_t gg = g + u;
-            if constexpr (WPL == 1) {
-              wv0[u][0] = ldg_stream(w0p + gg * WPG);
-              wv1[u][0] = ldg_stream(w1p + gg * WPG);
-            } else if constexpr (WPL == 2) {
-              uint2 a0 = ldg_stream(reinterpret_cast<const uint2*>(w0p + gg * WPG));
-              uint2 a1 = ldg_stream(reinterpret_cast<const uint2*>(w1p + gg * WPG));
-              wv0[u][0] = a0.x; wv0[u][1] = a0.y;
-              wv1[u][0] = a1.x; wv1[u][1] = a1.y;
-            } else {
-#pragma unroll
-              for (int q = 0; q < WPL; q += 4) {
-                uint4 a0 = ldg_stream(reinterpret_cast<const uint4*>(w0p + gg * WPG + q));
-                uint4 a1 = ldg_stream(reinterpret_cast<const uint4*>(w1p + gg * WPG + q));
-                wv0[u][q] = a0.x; wv0[u][q + 1] = a0.y; wv0[u][q + 2] = a0.z; wv0[u][q + 3] = a0.w;
-                wv1[u][q] = a1.x; wv1[u][q + 1] = a1.y; wv1[u][q + 2] = a1.z; wv1[u][q + 3] = a1.w;
-              }
-            }
-            sv0[u] = s0p[gg];
-            bv0[u] = b0p[gg];
-            sv1[u] = s1p[gg];
-            bv1[u] = b1p[gg];
+  if (warp == QMV_CWARPS) {
+    // ======================= producer warp (lane 0 issues) =======================
+    bool pend = false;
+    for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
+      const QmvItem I = qmv_item(p, mode, item, rowtiles);
+      if (I.ntok == 0) continue;
+      const int ybase = (int)(I.e * p.N + I.n0);  // row coordinate in the [E*N, .] maps
+      if (!I.zero_rows) {
+        const int slot = ic & 1;
+        const uint32_t use = ic >> 1;
+        ic++;
+        if (sc_tma && lane == 0) {
+          if (use > 0) ok &= mbar_wait(&scempty[slot], (use - 1) & 1);
+          mbar_arrive_expect_tx(&scfull[slot], 2u * QMV_ROWS * WS * 2);
+          tma_load_2d(scb + ((size_t)slot * 2 + 0) * QMV_ROWS * WS, &tms, xs0, ybase, &scfull[slot]);
+          tma_load_2d(scb + ((size_t)slot * 2 + 1) * QMV_ROWS * WS, &tmb, xs0, ybase, &scfull[slot]);
+        }
+      }
+      for (int64_t chunk = 0; chunk < I.ntok; chunk += TOKA) {
+        if (!I.zero_rows && lane == 0) {
+          for (int st = 0; st < nst; st++, it_stage++) {
+            const int slot = it_stage % QMV_STAGES;
+            const uint32_t use = it_stage / QMV_STAGES;
+            if (use > 0) ok &= mbar_wait(&empty[slot], (use - 1) & 1);
+            mbar_arrive_expect_tx(&full[slot], QMV_ROWS * 128);
+            tma_load_2d(ring + (size_t)slot * QMV_ROWS * 128, &tmw, (int)((gs0 + st * SG) * GB), ybase,
+                        &full[slot]);
           }
         }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          if (g + u < g1) {
-            const int64_t kbase = (g + u) * GS + c * VPL;
-            // Per group: ag = sum_k x*code (exact products, fp32 accumulate),
-            // xg = sum_k x (an MMA against an all-ones A tile), then
-            // y += scale*ag + bias*xg as MLX's qdot does (quantized.h:209-316).
-            float ag[NT][4], xg[NT][4];
-#pragma unroll
-            for (int t = 0; t < NT; t++)
-#pragma unroll
-              for (int i = 0; i < 4; i++) ag[t][i] = xg[t][i] = 0.f;
-#pragma unroll
-            for (int wi = 0; wi < WPL; wi++) {
-              if constexpr (BITS == 4) {
-                uint32_t p0[4], p1[4];
-                unpack4(wv0[u][wi], p0);
-                unpack4(wv1[u][wi], p1);
-                const uint32_t a0[4] = {p0[0], p1[0], p0[1], p1[1]};
-                const uint32_t a1[4] = {p0[2], p1[2], p0[3], p1[3]};
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
-                  uint32_t x02 = 0, x46 = 0, x13 = 0, x57 = 0;
-                  if (xr[t]) {
-                    uint4 xv = *reinterpret_cast<const uint4*>(xr[t] + kbase + wi * 8);
-                    x02 = prmt(xv.x, xv.y, 0x5410);
-                    x46 = prmt(xv.z, xv.w, 0x5410);
-                    x13 = prmt(xv.x, xv.y, 0x7632);
-                    x57 = prmt(xv.z, xv.w, 0x7632);
-                  }
-                  mma_bf16_16816(ag[t], a0, x02, x46);
-                  mma_bf16_16816(ag[t], a1, x13, x57);
-                  mma_bf16_16816(xg[t], kOnes, x02, x46);
-                  mma_bf16_16816(xg[t], kOnes, x13, x57);
-                }
-              } else {
-                uint32_t p0[2], p1[2];
-                unpack8(wv0[u][wi], p0);
-                unpack8(wv1[u][wi], p1);
-                const uint32_t a[4] = {p0[0], p1[0], p0[1], p1[1]};
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
-                  uint32_t x01 = 0, x23 = 0;
-                  if (xr[t]) {
-                    uint2 xv = *reinterpret_cast<const uint2*>(xr[t] + kbase + wi * 4);
-                    x01 = xv.x;
-                    x23 = xv.y;
-                  }
-                  mma_bf16_16816(ag[t], a, x01, x23);
-                  mma_bf16_16816(xg[t], kOnes, x01, x23);
-                }
-              }
-            }
-            const float s0 = __bfloat162float(sv0[u]), s1 = __bfloat162float(sv1[u]);
-            // 4-bit codes carry +128: fold -128*scale*sum(x) into the bias term
-            const float c0 = BITS == 4 ? fmaf(-128.f, s0, __bfloat162float(bv0[u])) : __bfloat162float(bv0[u]);
-            const float c1 = BITS == 4 ? fmaf(-128.f, s1, __bfloat162float(bv1[u])) : __bfloat162float(bv1[u]);
-#pragma unroll
-            for (int t = 0; t < NT; t++) {
-              acc[t][0] = fmaf(s0, ag[t][0], fmaf(c0, xg[t][0], acc[t][0]));
-              acc[t][1] = fmaf(s0, ag[t][1], fmaf(c0, xg[t][1], acc[t][1]));
-              acc[t][2] = fmaf(s1, ag[t][2], fmaf(c1, xg[t][2], acc[t][2]));
-              acc[t][3] = fmaf(s1, ag[t][3], fmaf(c1, xg[t][3], acc[t][3]));
-            }
-          }
+        __syncwarp();
+        if (C > 1) {  // one cluster-barrier phase per output tile; wait lazily to run ahead
+          if (pend) cluster_wait();
+          cluster_arrive();
+          pend = true;
         }
       }
     }
-
-    // ---- reduce the 8 warps' partial tiles and store bf16 ----
-#pragma unroll
-    for (int t = 0; t < NT; t++) {
-      red[warp][t * 8 + 2 * c][gq] = acc[t][0];
-      red[warp][t * 8 + 2 * c + 1][gq] = acc[t][1];
-      red[warp][t * 8 + 2 * c][gq + 8] = acc[t][2];
-      red[warp][t * 8 + 2 * c + 1][gq + 8] = acc[t][3];
+    if (C > 1) {
+      if (pend) cluster_wait();
+      cluster_arrive();
+      cluster_wait();
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < NT * 8 * QMV_ROWS; i += QMV_WARPS * 32) {
-      int tok = i / QMV_ROWS, r = i % QMV_ROWS;
-      if (tok < ntok && n0 + r < p.N) {
-        float s = 0.f;
+  } else {
+    // ======================= consumer warps =======================
+    const int gq = lane >> 2, c = lane & 3;
+    const int r0 = warp * 16 + gq, r1 = r0 + 8;
+    const int crow_lo = rank * QMV_ROWS / C, crow_hi = (rank + 1) * QMV_ROWS / C;
+    uint32_t red_count = 0;
+    bool x_staged = false;
+    for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
+      const QmvItem I = qmv_item(p, mode, item, rowtiles);
+      if (I.ntok == 0) continue;
+      int slot_sc = 0;
+      if (!I.zero_rows) {
+        slot_sc = ic & 1;
+        if (sc_tma) {
+          ok &= mbar_wait(&scfull[slot_sc], (ic >> 1) & 1);
+        } else {
+          // scales whose rows are not 16-byte strided: plain loads into the same layout
+          named_bar_sync(1, 32 * QMV_CWARPS);
+          for (int i = tid; i < 2 * QMV_ROWS * nG; i += 32 * QMV_CWARPS) {
+            const int kind = i / (QMV_ROWS * nG), rem = i - kind * QMV_ROWS * nG;
+            const int r = rem / nG, gl = rem - r * nG;
+            const int64_t row = I.e * p.N + (I.n0 + r < p.N ? I.n0 + r : p.N - 1);
+            scb[(((size_t)slot_sc * 2 + kind) * QMV_ROWS + r) * WS + soff + gl] =
+                (kind ? p.biases : p.scales)[row * KG + gs0 + gl];
+          }
+          named_bar_sync(1, 32 * QMV_CWARPS);
+        }
+        ic++;
+      }
+      const bf16* s0w = scb + (((size_t)slot_sc * 2 + 0) * QMV_ROWS + r0) * WS + soff;
+      const bf16* s1w = scb + (((size_t)slot_sc * 2 + 0) * QMV_ROWS + r1) * WS + soff;
+      const bf16* b0w = scb + (((size_t)slot_sc * 2 + 1) * QMV_ROWS + r0) * WS + soff;
+      const bf16* b1w = scb + (((size_t)slot_sc * 2 + 1) * QMV_ROWS + r1) * WS + soff;
+
+      for (int64_t chunk = 0; chunk < I.ntok; chunk += TOKA) {
+        const int ntok = (int)((I.ntok - chunk) < TOKA ? (I.ntok - chunk) : TOKA);
+        if (mode != QMV_DENSE || !x_staged || I.ntok > TOKA) {
+          // stage x of this chunk in fragment order, with per-group sums
+          named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous chunk
+          for (int it = tid; it < TOKA * nG; it += 32 * QMV_CWARPS) {
+            const int gl = it / TOKA, tok = it - gl * TOKA;
+            const bf16* xrow = nullptr;
+            if (tok < ntok && !I.zero_rows) {
+              bf16* yr_unused;
+              token_rows(p, mode, I.base, chunk + tok, xrow, yr_unused);
+              xrow += (gs0 + gl) * GS;
+            }
+            float sum = 0.f;
 #pragma unroll
-        for (int wv = 0; wv < QMV_WARPS; wv++) s += red[wv][tok][r];
-        const bf16* xr_unused;
-        bf16* yr;
-        token_rows(p, mode, base, chunk + tok, xr_unused, yr);
-        yr[n0 + r] = __float2bfloat16_rn(s);
+            for (int cc = 0; cc < 4; cc++) {
+#pragma unroll
+              for (int wi = 0; wi < WPL; wi++) {
+                uint8_t* dst = xfrag + ((((size_t)gl * WPL + wi) * TOKA + tok) * 4 + cc) * FB;
+                if constexpr (BITS == 4) {
+                  uint4 v = make_uint4(0, 0, 0, 0);
+                  if (xrow) v = *reinterpret_cast<const uint4*>(xrow + cc * VPL + wi * 8);
+                  uint4 f;
+                  f.x = prmt(v.x, v.y, 0x5410);  // (x0, x2)
+                  f.y = prmt(v.z, v.w, 0x5410);  // (x4, x6)
+                  f.z = prmt(v.x, v.y, 0x7632);  // (x1, x3)
+                  f.w = prmt(v.z, v.w, 0x7632);  // (x5, x7)
+                  *reinterpret_cast<uint4*>(dst) = f;
+                  const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
+                  const float2 c2 = __bfloat1622float2(u32_as_bf162(v.z)), d2 = __bfloat1622float2(u32_as_bf162(v.w));
+                  sum += ((a.x + a.y) + (b2.x + b2.y)) + ((c2.x + c2.y) + (d2.x + d2.y));
+                } else {
+                  uint2 v = make_uint2(0, 0);
+                  if (xrow) v = *reinterpret_cast<const uint2*>(xrow + cc * VPL + wi * 4);
+                  *reinterpret_cast<uint2*>(dst) = v;
+                  const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
+                  sum += (a.x + a.y) + (b2.x + b2.y);
+                }
+              }
+            }
+            xsum[gl * TOKA + tok] = sum;
+          }
+          named_bar_sync(1, 32 * QMV_CWARPS);
+          x_staged = true;
+        }
+
+        float acc[NT][4];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+        if (!I.zero_rows) {
+          for (int st = 0; st < nst; st++, it_stage++) {
+            const int slot = it_stage % QMV_STAGES;
+            ok &= mbar_wait(&full[slot], (it_stage / QMV_STAGES) & 1);
+            const int ng = (nG - st * SG) < SG ? (nG - st * SG) : SG;
+            const uint8_t* stg = ring + (size_t)slot * QMV_ROWS * 128;
+            for (int gi = 0; gi < ng; gi++) {
+              const int gl = st * SG + gi;
+              uint32_t wv0[WPL], wv1[WPL];
+#pragma unroll
+              for (int q = 0; q < WPL; q += (WPL < 4 ? WPL : 4)) {
+                const int o = gi * GB + c * WPL * 4 + q * 4;
+                if constexpr (WPL == 1) {
+                  wv0[q] = *reinterpret_cast<const uint32_t*>(stg + swz128(r0, o));
+                  wv1[q] = *reinterpret_cast<const uint32_t*>(stg + swz128(r1, o));
+                } else if constexpr (WPL == 2) {
+                  const uint2 a0 = *reinterpret_cast<const uint2*>(stg + swz128(r0, o));
+                  const uint2 a1 = *reinterpret_cast<const uint2*>(stg + swz128(r1, o));
+                  wv0[q] = a0.x; wv0[q + 1] = a0.y; wv1[q] = a1.x; wv1[q + 1] = a1.y;
+                } else {
+                  const uint4 a0 = *reinterpret_cast<const uint4*>(stg + swz128(r0, o));
+                  const uint4 a1 = *reinterpret_cast<const uint4*>(stg + swz128(r1, o));
+                  wv0[q] = a0.x; wv0[q + 1] = a0.y; wv0[q + 2] = a0.z; wv0[q + 3] = a0.w;
+                  wv1[q] = a1.x; wv1[q + 1] = a1.y; wv1[q + 2] = a1.z; wv1[q + 3] = a1.w;
+                }
+              }
+              float ag[NT][4];
+#pragma unroll
+              for (int t = 0; t < NT; t++) ag[t][0] = ag[t][1] = ag[t][2] = ag[t][3] = 0.f;
+#pragma unroll
+              for (int wi = 0; wi < WPL; wi++) {
+                const uint8_t* xf = xfrag + (((size_t)gl * WPL + wi) * TOKA * 4 + c) * FB;
+                if constexpr (BITS == 4) {
+                  uint32_t p0[4], p1[4];
+                  unpack4(wv0[wi], p0);
+                  unpack4(wv1[wi], p1);
+                  const uint32_t a0[4] = {p0[0], p1[0], p0[1], p1[1]};
+                  const uint32_t a1[4] = {p0[2], p1[2], p0[3], p1[3]};
+#pragma unroll
+                  for (int t = 0; t < NT; t++) {
+                    uint4 xv = make_uint4(0, 0, 0, 0);
+                    if (t * 8 + gq < ntok) xv = *reinterpret_cast<const uint4*>(xf + (size_t)(t * 8 + gq) * 4 * FB);
+                    mma_bf16_16816(ag[t], a0, xv.x, xv.y);
+                    mma_bf16_16816(ag[t], a1, xv.z, xv.w);
+                  }
+                } else {
+                  uint32_t p0[2], p1[2];
+                  unpack8(wv0[wi], p0);
+                  unpack8(wv1[wi], p1);
+                  const uint32_t a[4] = {p0[0], p1[0], p0[1], p1[1]};
+#pragma unroll
+                  for (int t = 0; t < NT; t++) {
+                    uint2 xv = make_uint2(0, 0);
+                    if (t * 8 + gq < ntok) xv = *reinterpret_cast<const uint2*>(xf + (size_t)(t * 8 + gq) * 4 * FB);
+                    mma_bf16_16816(ag[t], a, xv.x, xv.y);
+                  }
+                }
+              }
+              const float sc0 = __bfloat162float(s0w[gl]), sc1 = __bfloat162float(s1w[gl]);
+              const float bc0 = BITS == 4 ? fmaf(-128.f, sc0, __bfloat162float(b0w[gl])) : __bfloat162float(b0w[gl]);
+              const float bc1 = BITS == 4 ? fmaf(-128.f, sc1, __bfloat162float(b1w[gl])) : __bfloat162float(b1w[gl]);
+#pragma unroll
+              for (int t = 0; t < NT; t++) {
+                const int ta = t * 8 + 2 * c;
+                const float xa = ta < ntok ? xsum[gl * TOKA + ta] : 0.f;
+                const float xb = ta + 1 < ntok ? xsum[gl * TOKA + ta + 1] : 0.f;
+                acc[t][0] = fmaf(sc0, ag[t][0], fmaf(bc0, xa, acc[t][0]));
+                acc[t][1] = fmaf(sc0, ag[t][1], fmaf(bc0, xb, acc[t][1]));
+                acc[t][2] = fmaf(sc1, ag[t][2], fmaf(bc1, xa, acc[t][2]));
+                acc[t][3] = fmaf(sc1, ag[t][3], fmaf(bc1, xb, acc[t][3]));
+              }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+          }
+        }
+        // ---- output tile ----
+        if (C == 1) {
+#pragma unroll
+          for (int t = 0; t < NT; t++) {
+            const int ta = t * 8 + 2 * c;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const int tok = ta + (j & 1);
+              const int64_t row = I.n0 + (j < 2 ? r0 : r1);
+              if (tok < ntok && row < p.N) {
+                const bf16* xr_unused;
+                bf16* yr;
+                token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
+                yr[row] = __float2bfloat16_rn(acc[t][j]);
+              }
+            }
+          }
+        } else {
+          float* rb = red + (size_t)(red_count & 1) * QMV_ROWS * TOKA;
+#pragma unroll
+          for (int t = 0; t < NT; t++) {
+            const int ta = t * 8 + 2 * c;
+            if (ta < TOKA) { rb[r0 * TOKA + ta] = acc[t][0]; rb[r1 * TOKA + ta] = acc[t][2]; }
+            if (ta + 1 < TOKA) { rb[r0 * TOKA + ta + 1] = acc[t][1]; rb[r1 * TOKA + ta + 1] = acc[t][3]; }
+          }
+          cluster_arrive();
+          cluster_wait();
+          cg::cluster_group cluster = cg::this_cluster();
+          for (int i = tid; i < (crow_hi - crow_lo) * ntok; i += 32 * QMV_CWARPS) {
+            const int r = crow_lo + i / ntok, tok = i % ntok;
+            float s = 0.f;
+            for (int q = 0; q < C; q++) s += cluster.map_shared_rank(rb, q)[r * TOKA + tok];
+            if (I.n0 + r < p.N) {
+              const bf16* xr_unused;
+              bf16* yr;
+              token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
+              yr[I.n0 + r] = __float2bfloat16_rn(s);
+            }
+          }
+          red_count++;
+        }
+      }
+      if (!I.zero_rows && sc_tma) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&scempty[slot_sc]);
       }
     }
-    __syncthreads();
+    if (C > 1) {  // keep this CTA's shared memory alive until every peer has read it
+      cluster_arrive();
+      cluster_wait();
+    }
   }
+  if (!ok && p.status) atomicExch(p.status, VMLX_E_STATE);
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BITS, int GS, int NT>
+static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
+  auto kern = qmv_kernel<BITS, GS, NT>;
+  QmvPlan L;
+  L.init(BITS, GS, ks, toka);
+  static bool attr_set = false;  // per template instance
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return check_cuda(e, "qmv: cudaFuncSetAttribute");
+    attr_set = true;
+  }
+  const int64_t E = (mode == QMV_DENSE) ? 1 : a.n_experts;
+  const int64_t KG = a.K / GS;
+  CUtensorMap tmw, tms, tmb;
+  if (!make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)a.K * BITS / 8, (uint64_t)(E * a.N),
+                    (uint64_t)a.K * BITS / 8, 128, QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return VMLX_E_CUDA;
+  int sc_tma = ((KG * 2) % 16 == 0) && L.ws <= 256 && aligned(a.scales, 16) && aligned(a.biases, 16);
+  if (sc_tma) {
+    if (!make_tmap_2d(&tms, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.scales, (uint64_t)KG, (uint64_t)(E * a.N),
+                      (uint64_t)KG * 2, (uint32_t)L.ws, QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tmap_2d(&tmb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.biases, (uint64_t)KG, (uint64_t)(E * a.N),
+                      (uint64_t)KG * 2, (uint32_t)L.ws, QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return VMLX_E_CUDA;
+  } else {
+    tms = tmw;  // unused
+    tmb = tmw;
+  }
+  const int64_t rowtiles = (a.N + QMV_ROWS - 1) / QMV_ROWS;
+  const int64_t n_items = rowtiles * zcount;
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, QMV_THREADS, L.total);
+  if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+  int64_t max_clusters = (int64_t)sm_count() * per_sm / C;
+  if (max_clusters < 1) max_clusters = 1;
+  const int64_t n_clusters = n_items < max_clusters ? n_items : max_clusters;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_clusters * C), 1, 1);
+  cfg.blockDim = dim3(QMV_THREADS);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, a, tmw, tms, tmb, sc_tma, mode, ks, C, toka, rowtiles, n_items),
+                    "qmv_kernel launch");
 }
 
 template <int BITS, int GS>
-static void launch_qmv_nt(int nt, const QmvArgs& a, int mode, dim3 grid, cudaStream_t st) {
-  dim3 block(QMV_WARPS * 32);
+static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, cudaStream_t st) {
+  constexpr int SG = QT<BITS, GS>::SG;
+  const int64_t KG = a.K / GS;
+  const int64_t items = ((a.N + QMV_ROWS - 1) / QMV_ROWS) * zcount;
+  const int64_t target = 2 * (int64_t)sm_count();
+  int C = (int)((target + items - 1) / items);
+  C = C < 1 ? 1 : (C > QMV_MAX_CLUSTER ? QMV_MAX_CLUSTER : C);
+  while (C > 1 && (KG + C - 1) / C < SG) C--;  // no slice thinner than one stage
+  const size_t budget = 100 * 1024;          // leaves room for two CTAs per SM
+  auto smem_of = [&](int C_, int toka_) {
+    QmvPlan L;
+    L.init(BITS, GS, (int)((KG + C_ - 1) / C_), toka_);
+    return L.total;
+  };
+  while (smem_of(C, toka) > budget && C < QMV_MAX_CLUSTER && C < KG) C++;
+  while (smem_of(C, toka) > budget && toka > 8) toka -= 8;
+  if (smem_of(C, toka) > 227 * 1024)
+    return set_error(VMLX_E_UNSUPPORTED, "qmv: K=%lld too large for the shared-memory plan", (long long)a.K);
+  // whole stages per slice where possible, so no TMA box runs into the next slice
+  int ks = (int)((KG + C - 1) / C);
+  if (ks % SG && (int64_t)((ks + SG - 1) / SG * SG) * (C - 1) < KG) ks = (ks + SG - 1) / SG * SG;
+  C = (int)((KG + ks - 1) / ks);
+  const int nt = (toka + 7) / 8;
   switch (nt) {
-    case 1: qmv_kernel<BITS, GS, 1><<<grid, block, 0, st>>>(a, mode); break;
-    case 2: qmv_kernel<BITS, GS, 2><<<grid, block, 0, st>>>(a, mode); break;
-    case 3: qmv_kernel<BITS, GS, 3><<<grid, block, 0, st>>>(a, mode); break;
-    default: qmv_kernel<BITS, GS, 4><<<grid, block, 0, st>>>(a, mode); break;
+    case 1: return launch_qmv_t<BITS, GS, 1>(a, mode, zcount, ks, C, toka, st);
+    case 2: return launch_qmv_t<BITS, GS, 2>(a, mode, zcount, ks, C, toka, st);
+    case 3: return launch_qmv_t<BITS, GS, 3>(a, mode, zcount, ks, C, toka, st);
+    default: return launch_qmv_t<BITS, GS, 4>(a, mode, zcount, ks, C, toka, st);
   }
 }
 
-// Host launcher shared by the dense and gathered entry points.
-int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t grid_y, int nt,
-               cudaStream_t st) {
-  dim3 grid((unsigned)((a.N + QMV_ROWS - 1) / QMV_ROWS), (unsigned)grid_y);
-  if (grid.y > 65535) return set_error(VMLX_E_INVALID, "too many batch elements (%lld)", (long long)grid_y);
-  if (bits == 4 && gs == 32) launch_qmv_nt<4, 32>(nt, a, mode, grid, st);
-  else if (bits == 4 && gs == 64) launch_qmv_nt<4, 64>(nt, a, mode, grid, st);
-  else if (bits == 4 && gs == 128) launch_qmv_nt<4, 128>(nt, a, mode, grid, st);
-  else if (bits == 8 && gs == 32) launch_qmv_nt<8, 32>(nt, a, mode, grid, st);
-  else if (bits == 8 && gs == 64) launch_qmv_nt<8, 64>(nt, a, mode, grid, st);
-  else if (bits == 8 && gs == 128) launch_qmv_nt<8, 128>(nt, a, mode, grid, st);
-  else return set_error(VMLX_E_UNSUPPORTED, "matmul: bits=%d group_size=%d not supported", bits, gs);
-  return check_launch("qmv_kernel");
+// Host launcher shared by the dense and gathered entry points.  `toka` is the
+// number of token rows staged per pass (<= 32); zcount the number of
+// (batch element | expert) weight selections.
+int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int toka, cudaStream_t st) {
+  if (toka < 1) toka = 1;
+  if (toka > 32) toka = 32;
+  if (bits == 4 && gs == 32) return launch_qmv_bg<4, 32>(a, mode, zcount, toka, st);
+  if (bits == 4 && gs == 64) return launch_qmv_bg<4, 64>(a, mode, zcount, toka, st);
+  if (bits == 4 && gs == 128) return launch_qmv_bg<4, 128>(a, mode, zcount, toka, st);
+  if (bits == 8 && gs == 32) return launch_qmv_bg<8, 32>(a, mode, zcount, toka, st);
+  if (bits == 8 && gs == 64) return launch_qmv_bg<8, 64>(a, mode, zcount, toka, st);
+  if (bits == 8 && gs == 128) return launch_qmv_bg<8, 128>(a, mode, zcount, toka, st);
+  return set_error(VMLX_E_UNSUPPORTED, "matmul: bits=%d group_size=%d not supported", bits, gs);
 }
 
 }  // namespace vmlx
