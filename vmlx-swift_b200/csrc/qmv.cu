@@ -112,20 +112,22 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&p)[2]) {
 // on the number of token rows staged at once (tok).  The ring is 1024-byte
 // aligned (the 128-byte TMA swizzle atom).
 struct QmvPlan {
-  int ks, tok, ws, wpl, fb;
-  size_t o_ring, o_sc, o_bar, o_xfrag, o_xsum, o_red, total;
+  int ks, tok, tokx, ws, wpl, fb;
+  size_t o_ring, o_sc, o_sc2, o_bar, o_xfrag, o_xsum, o_red, total;
   __host__ __device__ void init(int bits, int gs, int ks_, int tok_) {
     ks = ks_;
     tok = tok_;
+    tokx = (tok + 7) / 8 * 8;  // xsum row stride: whole 8-token MMA tiles
     ws = ((ks + 7) + 7) / 8 * 8;  // scale window (elements), 16-byte multiple
     wpl = gs * bits / 128;
     fb = bits == 4 ? 16 : 8;
     o_ring = 0;
     o_sc = o_ring + (size_t)QMV_STAGES * QMV_ROWS * 128;
-    o_bar = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
+    o_sc2 = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
+    o_bar = o_sc2 + (size_t)QMV_ROWS * ks * 8;
     o_xfrag = o_bar + (2 * QMV_STAGES + 4) * sizeof(uint64_t);
     o_xsum = o_xfrag + (size_t)ks * wpl * tok * 4 * fb;
-    o_red = o_xsum + (((size_t)ks * tok * 4 + 15) / 16) * 16;
+    o_red = o_xsum + (((size_t)ks * tokx * 4 + 15) / 16) * 16;
     total = o_red + (size_t)2 * QMV_ROWS * tok * 4 + 1024;  // + alignment slack
   }
 };
@@ -195,6 +197,8 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   uint64_t* scempty = scfull + 2;
   uint8_t* xfrag = smem + L.o_xfrag;
   float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);
+  float2* sc2 = reinterpret_cast<float2*>(smem + L.o_sc2);  // per (row, group): (scale, bias')
+  const int TOKX = L.tokx;
   float* red = reinterpret_cast<float*>(smem + L.o_red);
 
   if (tid == 0) {
@@ -288,18 +292,33 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         }
         ic++;
       }
-      const bf16* s0w = scb + (((size_t)slot_sc * 2 + 0) * QMV_ROWS + r0) * WS + soff;
-      const bf16* s1w = scb + (((size_t)slot_sc * 2 + 0) * QMV_ROWS + r1) * WS + soff;
-      const bf16* b0w = scb + (((size_t)slot_sc * 2 + 1) * QMV_ROWS + r0) * WS + soff;
-      const bf16* b1w = scb + (((size_t)slot_sc * 2 + 1) * QMV_ROWS + r1) * WS + soff;
+      // (scale, bias') in fp32 per (row, group); bias' folds the +128 of 4-bit codes
+      named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous item's pairs
+      if (!I.zero_rows) {
+        const bf16* sb = scb + (size_t)slot_sc * 2 * QMV_ROWS * WS;
+        for (int i = tid; i < QMV_ROWS * nG; i += 32 * QMV_CWARPS) {
+          const int r = i / nG, gl = i - r * nG;
+          const float sv = __bfloat162float(sb[r * WS + soff + gl]);
+          const float bv = __bfloat162float(sb[(QMV_ROWS + r) * WS + soff + gl]);
+          sc2[r * Ks + gl] = make_float2(sv, BITS == 4 ? fmaf(-128.f, sv, bv) : bv);
+        }
+        if (sc_tma) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&scempty[slot_sc]);  // the TMA slot can be refilled now
+        }
+      }
+      named_bar_sync(1, 32 * QMV_CWARPS);
+      const float2* sc0p = sc2 + r0 * Ks;
+      const float2* sc1p = sc2 + r1 * Ks;
 
       for (int64_t chunk = 0; chunk < I.ntok; chunk += TOKA) {
         const int ntok = (int)((I.ntok - chunk) < TOKA ? (I.ntok - chunk) : TOKA);
         if (mode != QMV_DENSE || !x_staged || I.ntok > TOKA) {
           // stage x of this chunk in fragment order, with per-group sums
           named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous chunk
-          for (int it = tid; it < TOKA * nG; it += 32 * QMV_CWARPS) {
-            const int gl = it / TOKA, tok = it - gl * TOKA;
+          for (int it = tid; it < TOKX * nG; it += 32 * QMV_CWARPS) {
+            const int gl = it / TOKX, tok = it - gl * TOKX;
+            if (tok >= TOKA) { xsum[gl * TOKX + tok] = 0.f; continue; }
             const bf16* xrow = nullptr;
             if (tok < ntok && !I.zero_rows) {
               bf16* yr_unused;
@@ -333,7 +352,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 }
               }
             }
-            xsum[gl * TOKA + tok] = sum;
+            xsum[gl * TOKX + tok] = (tok < ntok) ? sum : 0.f;
           }
           named_bar_sync(1, 32 * QMV_CWARPS);
           x_staged = true;
@@ -342,76 +361,81 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         float acc[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+        bool tok_ok[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) tok_ok[t] = t * 8 + gq < ntok;
         if (!I.zero_rows) {
           for (int st = 0; st < nst; st++, it_stage++) {
             const int slot = it_stage % QMV_STAGES;
             ok &= mbar_wait(&full[slot], (it_stage / QMV_STAGES) & 1);
             const int ng = (nG - st * SG) < SG ? (nG - st * SG) : SG;
-            const uint8_t* stg = ring + (size_t)slot * QMV_ROWS * 128;
-            for (int gi = 0; gi < ng; gi++) {
-              const int gl = st * SG + gi;
-              uint32_t wv0[WPL], wv1[WPL];
+            const uint8_t* stg0 = ring + (size_t)slot * QMV_ROWS * 128 + r0 * 128;
+            const uint8_t* stg1 = stg0 + 8 * 128;  // row r1 = r0 + 8 has the same swizzle phase
+            const uint8_t* xst = xfrag + ((st * SG * WPL) * TOKA * 4 + gq * 4 + c) * FB;
 #pragma unroll
-              for (int q = 0; q < WPL; q += (WPL < 4 ? WPL : 4)) {
-                const int o = gi * GB + c * WPL * 4 + q * 4;
-                if constexpr (WPL == 1) {
-                  wv0[q] = *reinterpret_cast<const uint32_t*>(stg + swz128(r0, o));
-                  wv1[q] = *reinterpret_cast<const uint32_t*>(stg + swz128(r1, o));
-                } else if constexpr (WPL == 2) {
-                  const uint2 a0 = *reinterpret_cast<const uint2*>(stg + swz128(r0, o));
-                  const uint2 a1 = *reinterpret_cast<const uint2*>(stg + swz128(r1, o));
-                  wv0[q] = a0.x; wv0[q + 1] = a0.y; wv1[q] = a1.x; wv1[q + 1] = a1.y;
-                } else {
-                  const uint4 a0 = *reinterpret_cast<const uint4*>(stg + swz128(r0, o));
-                  const uint4 a1 = *reinterpret_cast<const uint4*>(stg + swz128(r1, o));
-                  wv0[q] = a0.x; wv0[q + 1] = a0.y; wv0[q + 2] = a0.z; wv0[q + 3] = a0.w;
-                  wv1[q] = a1.x; wv1[q + 1] = a1.y; wv1[q + 2] = a1.z; wv1[q + 3] = a1.w;
-                }
-              }
-              float ag[NT][4];
+            for (int gi = 0; gi < SG; gi++) {
+              if (gi < ng) {
+                const int gl = st * SG + gi;
+                uint32_t wv0[WPL], wv1[WPL];
 #pragma unroll
-              for (int t = 0; t < NT; t++) ag[t][0] = ag[t][1] = ag[t][2] = ag[t][3] = 0.f;
-#pragma unroll
-              for (int wi = 0; wi < WPL; wi++) {
-                const uint8_t* xf = xfrag + (((size_t)gl * WPL + wi) * TOKA * 4 + c) * FB;
-                if constexpr (BITS == 4) {
-                  uint32_t p0[4], p1[4];
-                  unpack4(wv0[wi], p0);
-                  unpack4(wv1[wi], p1);
-                  const uint32_t a0[4] = {p0[0], p1[0], p0[1], p1[1]};
-                  const uint32_t a1[4] = {p0[2], p1[2], p0[3], p1[3]};
-#pragma unroll
-                  for (int t = 0; t < NT; t++) {
-                    uint4 xv = make_uint4(0, 0, 0, 0);
-                    if (t * 8 + gq < ntok) xv = *reinterpret_cast<const uint4*>(xf + (size_t)(t * 8 + gq) * 4 * FB);
-                    mma_bf16_16816(ag[t], a0, xv.x, xv.y);
-                    mma_bf16_16816(ag[t], a1, xv.z, xv.w);
-                  }
-                } else {
-                  uint32_t p0[2], p1[2];
-                  unpack8(wv0[wi], p0);
-                  unpack8(wv1[wi], p1);
-                  const uint32_t a[4] = {p0[0], p1[0], p0[1], p1[1]};
-#pragma unroll
-                  for (int t = 0; t < NT; t++) {
-                    uint2 xv = make_uint2(0, 0);
-                    if (t * 8 + gq < ntok) xv = *reinterpret_cast<const uint2*>(xf + (size_t)(t * 8 + gq) * 4 * FB);
-                    mma_bf16_16816(ag[t], a, xv.x, xv.y);
+                for (int q = 0; q < WPL; q += (WPL < 4 ? WPL : 4)) {
+                  const int o = gi * GB + c * WPL * 4 + q * 4;
+                  const int so = ((((o >> 4) ^ gq)) << 4) + (o & 15);  // 128B swizzle: chunk ^ (row & 7)
+                  if constexpr (WPL == 1) {
+                    wv0[q] = *reinterpret_cast<const uint32_t*>(stg0 + so);
+                    wv1[q] = *reinterpret_cast<const uint32_t*>(stg1 + so);
+                  } else if constexpr (WPL == 2) {
+                    const uint2 a0 = *reinterpret_cast<const uint2*>(stg0 + so);
+                    const uint2 a1 = *reinterpret_cast<const uint2*>(stg1 + so);
+                    wv0[q] = a0.x; wv0[q + 1] = a0.y; wv1[q] = a1.x; wv1[q + 1] = a1.y;
+                  } else {
+                    const uint4 a0 = *reinterpret_cast<const uint4*>(stg0 + so);
+                    const uint4 a1 = *reinterpret_cast<const uint4*>(stg1 + so);
+                    wv0[q] = a0.x; wv0[q + 1] = a0.y; wv0[q + 2] = a0.z; wv0[q + 3] = a0.w;
+                    wv1[q] = a1.x; wv1[q + 1] = a1.y; wv1[q + 2] = a1.z; wv1[q + 3] = a1.w;
                   }
                 }
-              }
-              const float sc0 = __bfloat162float(s0w[gl]), sc1 = __bfloat162float(s1w[gl]);
-              const float bc0 = BITS == 4 ? fmaf(-128.f, sc0, __bfloat162float(b0w[gl])) : __bfloat162float(b0w[gl]);
-              const float bc1 = BITS == 4 ? fmaf(-128.f, sc1, __bfloat162float(b1w[gl])) : __bfloat162float(b1w[gl]);
+                float ag[NT][4];
 #pragma unroll
-              for (int t = 0; t < NT; t++) {
-                const int ta = t * 8 + 2 * c;
-                const float xa = ta < ntok ? xsum[gl * TOKA + ta] : 0.f;
-                const float xb = ta + 1 < ntok ? xsum[gl * TOKA + ta + 1] : 0.f;
-                acc[t][0] = fmaf(sc0, ag[t][0], fmaf(bc0, xa, acc[t][0]));
-                acc[t][1] = fmaf(sc0, ag[t][1], fmaf(bc0, xb, acc[t][1]));
-                acc[t][2] = fmaf(sc1, ag[t][2], fmaf(bc1, xa, acc[t][2]));
-                acc[t][3] = fmaf(sc1, ag[t][3], fmaf(bc1, xb, acc[t][3]));
+                for (int t = 0; t < NT; t++) ag[t][0] = ag[t][1] = ag[t][2] = ag[t][3] = 0.f;
+#pragma unroll
+                for (int wi = 0; wi < WPL; wi++) {
+                  const uint8_t* xf = xst + ((gi * WPL + wi) * TOKA * 4) * FB;
+                  if constexpr (BITS == 4) {
+                    uint32_t p0[4], p1[4];
+                    unpack4(wv0[wi], p0);
+                    unpack4(wv1[wi], p1);
+                    const uint32_t a0[4] = {p0[0], p1[0], p0[1], p1[1]};
+                    const uint32_t a1[4] = {p0[2], p1[2], p0[3], p1[3]};
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                      uint4 xv = make_uint4(0, 0, 0, 0);
+                      if (tok_ok[t]) xv = *reinterpret_cast<const uint4*>(xf + t * 32 * FB);
+                      mma_bf16_16816(ag[t], a0, xv.x, xv.y);
+                      mma_bf16_16816(ag[t], a1, xv.z, xv.w);
+                    }
+                  } else {
+                    uint32_t p0[2], p1[2];
+                    unpack8(wv0[wi], p0);
+                    unpack8(wv1[wi], p1);
+                    const uint32_t a[4] = {p0[0], p1[0], p0[1], p1[1]};
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                      uint2 xv = make_uint2(0, 0);
+                      if (tok_ok[t]) xv = *reinterpret_cast<const uint2*>(xf + t * 32 * FB);
+                      mma_bf16_16816(ag[t], a, xv.x, xv.y);
+                    }
+                  }
+                }
+                const float2 sb0 = sc0p[gl], sb1 = sc1p[gl];
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                  const float2 xs = *reinterpret_cast<const float2*>(xsum + gl * TOKX + t * 8 + 2 * c);
+                  acc[t][0] = fmaf(sb0.x, ag[t][0], fmaf(sb0.y, xs.x, acc[t][0]));
+                  acc[t][1] = fmaf(sb0.x, ag[t][1], fmaf(sb0.y, xs.y, acc[t][1]));
+                  acc[t][2] = fmaf(sb1.x, ag[t][2], fmaf(sb1.y, xs.x, acc[t][2]));
+                  acc[t][3] = fmaf(sb1.x, ag[t][3], fmaf(sb1.y, xs.y, acc[t][3]));
+                }
               }
             }
             __syncwarp();
@@ -459,10 +483,6 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           }
           red_count++;
         }
-      }
-      if (!I.zero_rows && sc_tma) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&scempty[slot_sc]);
       }
     }
     if (C > 1) {  // keep this CTA's shared memory alive until every peer has read it
@@ -537,28 +557,46 @@ static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
                     "qmv_kernel launch");
 }
 
+// K-slice width for a cluster of C CTAs: whole stages of groups where the
+// rounding does not leave a slice empty.
+static int slice_groups(int64_t KG, int C, int SG) {
+  int ks = (int)((KG + C - 1) / C);
+  if (ks % SG && (int64_t)((ks + SG - 1) / SG * SG) * (C - 1) < KG) ks = (ks + SG - 1) / SG * SG;
+  return ks;
+}
+
 template <int BITS, int GS>
 static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, cudaStream_t st) {
   constexpr int SG = QT<BITS, GS>::SG;
   const int64_t KG = a.K / GS;
   const int64_t items = ((a.N + QMV_ROWS - 1) / QMV_ROWS) * zcount;
-  const int64_t target = 2 * (int64_t)sm_count();
-  int C = (int)((target + items - 1) / items);
-  C = C < 1 ? 1 : (C > QMV_MAX_CLUSTER ? QMV_MAX_CLUSTER : C);
-  while (C > 1 && (KG + C - 1) / C < SG) C--;  // no slice thinner than one stage
-  const size_t budget = 100 * 1024;          // leaves room for two CTAs per SM
-  auto smem_of = [&](int C_, int toka_) {
+  auto smem_of = [&](int ks_, int toka_) {
     QmvPlan L;
-    L.init(BITS, GS, (int)((KG + C_ - 1) / C_), toka_);
+    L.init(BITS, GS, ks_, toka_);
     return L.total;
   };
-  while (smem_of(C, toka) > budget && C < QMV_MAX_CLUSTER && C < KG) C++;
-  while (smem_of(C, toka) > budget && toka > 8) toka -= 8;
-  if (smem_of(C, toka) > 227 * 1024)
+  // Pick the cluster size that minimises the busiest cluster's work:
+  // ceil(items / resident clusters) * groups per slice.  Persistent clusters
+  // loop over items, so a grid one item past a full wave doubles the time.
+  int bestC = 1;
+  double best = 1e30;
+  for (int C = 1; C <= QMV_MAX_CLUSTER && C <= KG; C++) {
+    const int ks = slice_groups(KG, C, SG);
+    if ((KG + ks - 1) / ks != C) continue;  // this C rounds to another one
+    const size_t sm = smem_of(ks, toka);
+    if (sm > 227 * 1024) continue;
+    int per_sm = (int)((228 * 1024) / (sm + 1024));
+    per_sm = per_sm > 3 ? 3 : (per_sm < 1 ? 1 : per_sm);  // 160 threads x ~128 registers
+    const int64_t clusters = (int64_t)sm_count() * per_sm / C;
+    if (clusters < 1) continue;
+    const double cost = (double)((items + clusters - 1) / clusters) * ks + 0.25 * C;
+    if (cost < best) { best = cost; bestC = C; }
+  }
+  int C = bestC;
+  int ks = slice_groups(KG, C, SG);
+  while (smem_of(ks, toka) > 227 * 1024 && toka > 8) toka -= 8;
+  if (smem_of(ks, toka) > 227 * 1024)
     return set_error(VMLX_E_UNSUPPORTED, "qmv: K=%lld too large for the shared-memory plan", (long long)a.K);
-  // whole stages per slice where possible, so no TMA box runs into the next slice
-  int ks = (int)((KG + C - 1) / C);
-  if (ks % SG && (int64_t)((ks + SG - 1) / SG * SG) * (C - 1) < KG) ks = (ks + SG - 1) / SG * SG;
   C = (int)((KG + ks - 1) / ks);
   const int nt = (toka + 7) / 8;
   switch (nt) {
