@@ -60,6 +60,19 @@ VMLX_API const char* vmlx_last_error(void);
 VMLX_API int vmlx_version(void);
 
 /*
+ * Launch overlap (programmatic dependent launch) for the streaming kernels:
+ * when enabled, a quantized_matmul / gather_qmm grid may start streaming its
+ * weights, scales and biases while the previous kernel in the same stream is
+ * still running; it waits for that kernel before reading x or writing y.
+ * Enable it only when the weights, scales and biases of a call are never
+ * written by the kernel launched just before it in the same stream (true for
+ * inference with loaded weights).  Off by default.  Process-wide; returns the
+ * previous setting.  No counterpart in the reference (MLX schedules its own
+ * command buffers).
+ */
+VMLX_API int vmlx_set_launch_overlap(int enable);
+
+/*
  * Affine quantization of a row-major matrix w [rows, cols].
  * Replaces mlx_quantize (Source/Cmlx/include/mlx/c/ops.h:801-808) for
  * mode "affine"; arithmetic of affine_quantize

@@ -103,3 +103,10 @@ def test_consecutive_broadcast_rule(vm):
     assert f((1,), (6,))
     assert not f((8,), (4, 8))
     assert not f((1, 8), (4, 8))
+
+
+def test_launch_overlap_setter_returns_previous(vm):
+    lib = vm.lib()
+    prev = lib.vmlx_set_launch_overlap(1)
+    assert lib.vmlx_set_launch_overlap(0) == 1
+    assert lib.vmlx_set_launch_overlap(prev) == 0

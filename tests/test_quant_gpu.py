@@ -206,3 +206,28 @@ def test_switch_glu_qwen3_moe_shape(vm, orc, cuda, T):
     ref = orc.switch_glu(xb, hostw(gate), hostw(up), hostw(down), inds)
     assert y.shape == (T, k, D)
     check_close(y.float().cpu().numpy(), ref)
+
+
+def test_launch_overlap_chain_matches(vm, orc, cuda):
+    """Programmatic launch overlap: a chain of GEMVs where each call's x is the
+    previous call's y must give bit-identical results with overlap on and off."""
+    K = 2048
+    mats = [make_weights(orc, vm, cuda, K, K, 64, 4, 80 + i)[1] for i in range(4)]
+    x0 = torch.randn(2, K, device=cuda).bfloat16()
+
+    def chain():
+        x = x0
+        for _ in range(3):
+            for m in mats:
+                x = vm.quantized_mm(x, *m)
+        return x
+    lib = vm.lib()
+    prev = lib.vmlx_set_launch_overlap(0)
+    try:
+        ref = chain()
+        lib.vmlx_set_launch_overlap(1)
+        got = chain()
+        torch.cuda.synchronize()
+    finally:
+        lib.vmlx_set_launch_overlap(prev)
+    assert torch.equal(ref, got)

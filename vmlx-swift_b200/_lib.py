@@ -37,6 +37,7 @@ _sz = _c.c_size_t
 SIGNATURES = {
     "vmlx_last_error": (_str, []),
     "vmlx_version": (_int, []),
+    "vmlx_set_launch_overlap": (_int, [_int]),
     "vmlx_cuda_quantize": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _int, _int, _str, _vp]),
     "vmlx_cuda_dequantize": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, _i64, _int, _int, _str, _vp]),
     "vmlx_cuda_quantized_matmul": (

@@ -1,4 +1,5 @@
 // api.cu -- error reporting and version of the C ABI.
+#include <atomic>
 #include <string>
 
 #include "common.cuh"
@@ -19,8 +20,16 @@ int set_error(int code, const char* fmt, ...) {
 
 void clear_error() { g_last_error.clear(); }
 
+static std::atomic<int> g_overlap{0};
+bool launch_overlap() { return g_overlap.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace vmlx
 
 extern "C" const char* vmlx_last_error(void) { return vmlx::g_last_error.c_str(); }
 
 extern "C" int vmlx_version(void) { return 100; }
+
+extern "C" int vmlx_set_launch_overlap(int enable) {
+  int prev = vmlx::g_overlap.exchange(enable ? 1 : 0);
+  return prev;
+}

@@ -21,6 +21,9 @@ typedef __nv_bfloat162 bf162;
 int set_error(int code, const char* fmt, ...);
 void clear_error();
 
+// Programmatic dependent launch of the streaming kernels (vmlx_set_launch_overlap).
+bool launch_overlap();
+
 inline bool mode_is_affine(const char* mode) {
   return mode == nullptr || mode[0] == 0 || std::strcmp(mode, "affine") == 0;
 }

@@ -33,6 +33,7 @@
 #include "kernels.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
+#include <cstdlib>
 
 namespace vmlx {
 
@@ -43,6 +44,9 @@ constexpr int QMV_ROWS = 16 * QMV_CWARPS;     // rows per work item
 constexpr int QMV_THREADS = 32 * (QMV_CWARPS + 1);
 constexpr int QMV_STAGES = 6;
 constexpr int QMV_MAX_CLUSTER = 8;
+#ifndef QMV_PROBE
+#define QMV_PROBE 0  // experiment switch: 1 = skip the math, 2 = skip the cluster reduction
+#endif
 
 template <int BITS, int GS>
 struct QT {
@@ -113,7 +117,7 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&p)[2]) {
 // aligned (the 128-byte TMA swizzle atom).
 struct QmvPlan {
   int ks, tok, tokx, ws, wpl, fb;
-  size_t o_ring, o_sc, o_sc2, o_bar, o_xfrag, o_xsum, o_red, total;
+  size_t o_ring, o_sc, o_bar, o_xfrag, o_xsum, o_red, total;
   __host__ __device__ void init(int bits, int gs, int ks_, int tok_) {
     ks = ks_;
     tok = tok_;
@@ -123,8 +127,7 @@ struct QmvPlan {
     fb = bits == 4 ? 16 : 8;
     o_ring = 0;
     o_sc = o_ring + (size_t)QMV_STAGES * QMV_ROWS * 128;
-    o_sc2 = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
-    o_bar = o_sc2 + (size_t)QMV_ROWS * ks * 8;
+    o_bar = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
     o_xfrag = o_bar + (2 * QMV_STAGES + 4) * sizeof(uint64_t);
     o_xsum = o_xfrag + (size_t)ks * wpl * tok * 4 * fb;
     o_red = o_xsum + (((size_t)ks * tokx * 4 + 15) / 16) * 16;
@@ -197,7 +200,6 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   uint64_t* scempty = scfull + 2;
   uint8_t* xfrag = smem + L.o_xfrag;
   float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);
-  float2* sc2 = reinterpret_cast<float2*>(smem + L.o_sc2);  // per (row, group): (scale, bias')
   const int TOKX = L.tokx;
   float* red = reinterpret_cast<float*>(smem + L.o_red);
 
@@ -217,6 +219,9 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     if (sc_tma) { tma_prefetch_desc(&tms); tma_prefetch_desc(&tmb); }
   }
   __syncthreads();
+  // Let the next kernel in the stream launch now (when launch overlap is on):
+  // its producer may start streaming its own weights while this grid drains.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   bool ok = true;
   uint32_t it_stage = 0, ic = 0;
@@ -270,6 +275,9 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     const int crow_lo = rank * QMV_ROWS / C, crow_hi = (rank + 1) * QMV_ROWS / C;
     uint32_t red_count = 0;
     bool x_staged = false;
+    // x and y may be produced / consumed by the previous kernel: wait for it
+    // (a no-op unless this grid was launched with programmatic overlap).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);
       if (I.ntok == 0) continue;
@@ -293,23 +301,12 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         ic++;
       }
       // (scale, bias') in fp32 per (row, group); bias' folds the +128 of 4-bit codes
-      named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous item's pairs
-      if (!I.zero_rows) {
-        const bf16* sb = scb + (size_t)slot_sc * 2 * QMV_ROWS * WS;
-        for (int i = tid; i < QMV_ROWS * nG; i += 32 * QMV_CWARPS) {
-          const int r = i / nG, gl = i - r * nG;
-          const float sv = __bfloat162float(sb[r * WS + soff + gl]);
-          const float bv = __bfloat162float(sb[(QMV_ROWS + r) * WS + soff + gl]);
-          sc2[r * Ks + gl] = make_float2(sv, BITS == 4 ? fmaf(-128.f, sv, bv) : bv);
-        }
-        if (sc_tma) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&scempty[slot_sc]);  // the TMA slot can be refilled now
-        }
-      }
-      named_bar_sync(1, 32 * QMV_CWARPS);
-      const float2* sc0p = sc2 + r0 * Ks;
-      const float2* sc1p = sc2 + r1 * Ks;
+      // this lane's two rows of the item's bf16 scale / bias windows
+      const bf16* sbase = scb + (size_t)slot_sc * 2 * QMV_ROWS * WS;
+      const bf16* s0p = sbase + r0 * WS + soff;
+      const bf16* s1p = sbase + r1 * WS + soff;
+      const bf16* b0p = sbase + (QMV_ROWS + r0) * WS + soff;
+      const bf16* b1p = sbase + (QMV_ROWS + r1) * WS + soff;
 
       for (int64_t chunk = 0; chunk < I.ntok; chunk += TOKA) {
         const int ntok = (int)((I.ntok - chunk) < TOKA ? (I.ntok - chunk) : TOKA);
@@ -374,7 +371,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
             const uint8_t* xst = xfrag + ((st * SG * WPL) * TOKA * 4 + gq * 4 + c) * FB;
 #pragma unroll
             for (int gi = 0; gi < SG; gi++) {
-              if (gi < ng) {
+              if (gi < ng && QMV_PROBE != 1) {
                 const int gl = st * SG + gi;
                 uint32_t wv0[WPL], wv1[WPL];
 #pragma unroll
@@ -427,7 +424,11 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                     }
                   }
                 }
-                const float2 sb0 = sc0p[gl], sb1 = sc1p[gl];
+                float2 sb0, sb1;  // (scale, bias'): bias' folds the +128 of 4-bit codes
+                sb0.x = __bfloat162float(s0p[gl]);
+                sb1.x = __bfloat162float(s1p[gl]);
+                sb0.y = BITS == 4 ? fmaf(-128.f, sb0.x, __bfloat162float(b0p[gl])) : __bfloat162float(b0p[gl]);
+                sb1.y = BITS == 4 ? fmaf(-128.f, sb1.x, __bfloat162float(b1p[gl])) : __bfloat162float(b1p[gl]);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                   const float2 xs = *reinterpret_cast<const float2*>(xsum + gl * TOKX + t * 8 + 2 * c);
@@ -470,7 +471,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           cluster_arrive();
           cluster_wait();
           cg::cluster_group cluster = cg::this_cluster();
-          for (int i = tid; i < (crow_hi - crow_lo) * ntok; i += 32 * QMV_CWARPS) {
+          for (int i = tid; QMV_PROBE != 2 && i < (crow_hi - crow_lo) * ntok; i += 32 * QMV_CWARPS) {
             const int r = crow_lo + i / ntok, tok = i % ntok;
             float s = 0.f;
             for (int q = 0; q < C; q++) s += cluster.map_shared_rank(rb, q)[r * TOKA + tok];
@@ -483,6 +484,10 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           }
           red_count++;
         }
+      }
+      if (!I.zero_rows && sc_tma) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&scempty[slot_sc]);
       }
     }
     if (C > 1) {  // keep this CTA's shared memory alive until every peer has read it
@@ -546,13 +551,15 @@ static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   cfg.blockDim = dim3(QMV_THREADS);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = launch_overlap() ? 2 : 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, a, tmw, tms, tmb, sc_tma, mode, ks, C, toka, rowtiles, n_items),
                     "qmv_kernel launch");
 }
@@ -593,6 +600,9 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     if (cost < best) { best = cost; bestC = C; }
   }
   int C = bestC;
+#ifdef QMV_FORCE_C
+  if (getenv("QMV_FORCE_C")) C = atoi(getenv("QMV_FORCE_C"));
+#endif
   int ks = slice_groups(KG, C, SG);
   while (smem_of(ks, toka) > 227 * 1024 && toka > 8) toka -= 8;
   if (smem_of(ks, toka) > 227 * 1024)
