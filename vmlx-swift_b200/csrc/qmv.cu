@@ -33,7 +33,6 @@
 #include "kernels.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
-#include <cstdlib>
 
 namespace vmlx {
 
@@ -44,9 +43,7 @@ constexpr int QMV_ROWS = 16 * QMV_CWARPS;     // rows per work item
 constexpr int QMV_THREADS = 32 * (QMV_CWARPS + 1);
 constexpr int QMV_STAGES = 6;
 constexpr int QMV_MAX_CLUSTER = 8;
-#ifndef QMV_PROBE
-#define QMV_PROBE 0  // experiment switch: 1 = skip the math, 2 = skip the cluster reduction
-#endif
+
 
 template <int BITS, int GS>
 struct QT {
@@ -112,13 +109,35 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t (&p)[2]) {
   p[1] = bf162_as_u32(__floats2bfloat162_rn(f2, f3));
 }
 
+__device__ __forceinline__ unsigned long long pack_f2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long pack_u2(uint32_t a, uint32_t b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float2 unpack_f2(unsigned long long v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+// acc.xy += a.xy * b.xy (packed fp32 FMA, sm_100)
+__device__ __forceinline__ void ffma2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
 // Shared-memory plan of one CTA; sizes depend on the K-slice (ks groups) and
 // on the number of token rows staged at once (tok).  The ring is 1024-byte
 // aligned (the 128-byte TMA swizzle atom).
 struct QmvPlan {
   int ks, tok, tokx, ws, wpl, fb;
   size_t o_ring, o_sc, o_bar, o_xfrag, o_xsum, o_red, total;
-  __host__ __device__ void init(int bits, int gs, int ks_, int tok_) {
+  // cc: CUDA-core consumer (4-bit, <= 4 tokens): x staged as fp32 per 16-byte
+  // weight chunk (32 values) with per-chunk sums instead of MMA fragments.
+  __host__ __device__ void init(int bits, int gs, int ks_, int tok_, bool cc = false) {
     ks = ks_;
     tok = tok_;
     tokx = (tok + 7) / 8 * 8;  // xsum row stride: whole 8-token MMA tiles
@@ -129,8 +148,9 @@ struct QmvPlan {
     o_sc = o_ring + (size_t)QMV_STAGES * QMV_ROWS * 128;
     o_bar = o_sc + (size_t)2 * 2 * QMV_ROWS * ws * 2;
     o_xfrag = o_bar + (2 * QMV_STAGES + 4) * sizeof(uint64_t);
-    o_xsum = o_xfrag + (size_t)ks * wpl * tok * 4 * fb;
-    o_red = o_xsum + (((size_t)ks * tokx * 4 + 15) / 16) * 16;
+    const size_t nchunks = (size_t)ks * (gs * bits / 8) / 16;
+    o_xsum = o_xfrag + (cc ? nchunks * (tok * 32 + 4) * 4 : (size_t)ks * wpl * tok * 4 * fb);
+    o_red = o_xsum + (((cc ? nchunks * tok : (size_t)ks * tokx) * 4 + 15) / 16) * 16;
     total = o_red + (size_t)2 * QMV_ROWS * tok * 4 + 1024;  // + alignment slack
   }
 };
@@ -169,7 +189,7 @@ __device__ __forceinline__ uint32_t swz128(int r, int o) {
   return (uint32_t)(r * 128 + ((((o >> 4) ^ (r & 7))) << 4) + (o & 15));
 }
 
-template <int BITS, int GS, int NT>
+template <int BITS, int GS, int NT, bool CC>
 __global__ void __launch_bounds__(QMV_THREADS, 1)
 qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
            const __grid_constant__ CUtensorMap tmb, int sc_tma, int mode, int Ks, int C, int TOKA,
@@ -178,9 +198,13 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   constexpr int WPL = T::WPL, VPL = T::VPL, GB = T::GB, SG = T::SG, FB = T::FB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  static_assert(!CC || BITS == 4, "the CUDA-core consumer is 4-bit only");
   QmvPlan L;
-  L.init(BITS, GS, Ks, TOKA);
+  L.init(BITS, GS, Ks, TOKA, CC);
   const int WS = L.ws;
+  constexpr int CPS = 128 / 16;     // 16-byte chunks per row per stage
+  constexpr int CPG = GB / 16;      // chunks per group
+  const int XST = TOKA * 32 + 4;    // fp32 x stride per chunk (CUDA-core path), padded
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = (int)(blockIdx.x % C);  // K-slice == rank in the cluster (cluster dims (C,1,1))
@@ -199,6 +223,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   uint64_t* scfull = empty + QMV_STAGES;
   uint64_t* scempty = scfull + 2;
   uint8_t* xfrag = smem + L.o_xfrag;
+  float* xfrag_f = reinterpret_cast<float*>(xfrag);
   float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);
   const int TOKX = L.tokx;
   float* red = reinterpret_cast<float*>(smem + L.o_red);
@@ -313,6 +338,32 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         if (mode != QMV_DENSE || !x_staged || I.ntok > TOKA) {
           // stage x of this chunk in fragment order, with per-group sums
           named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous chunk
+          if constexpr (CC) {
+            // fp32 x, 32 values per 16-byte weight chunk, plus the chunk's sum
+            const int nch = nG * CPG;
+            for (int it = tid; it < TOKA * nch; it += 32 * QMV_CWARPS) {
+              const int ci = it / TOKA, tok = it - ci * TOKA;
+              const bf16* xrow = nullptr;
+              if (tok < ntok && !I.zero_rows) {
+                bf16* yr_unused;
+                token_rows(p, mode, I.base, chunk + tok, xrow, yr_unused);
+                xrow += gs0 * GS + ci * 32;
+              }
+              float* dst = xfrag_f + (size_t)ci * XST + tok * 32;
+              float sum = 0.f;
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (xrow) v = *reinterpret_cast<const uint4*>(xrow + q * 8);
+                const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
+                const float2 c2 = __bfloat1622float2(u32_as_bf162(v.z)), d2 = __bfloat1622float2(u32_as_bf162(v.w));
+                reinterpret_cast<float4*>(dst + q * 8)[0] = make_float4(a.x, a.y, b2.x, b2.y);
+                reinterpret_cast<float4*>(dst + q * 8)[1] = make_float4(c2.x, c2.y, d2.x, d2.y);
+                sum += ((a.x + a.y) + (b2.x + b2.y)) + ((c2.x + c2.y) + (d2.x + d2.y));
+              }
+              xsum[ci * TOKA + tok] = sum;
+            }
+          } else
           for (int it = tid; it < TOKX * nG; it += 32 * QMV_CWARPS) {
             const int gl = it / TOKX, tok = it - gl * TOKX;
             if (tok >= TOKA) { xsum[gl * TOKX + tok] = 0.f; continue; }
@@ -355,6 +406,8 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           x_staged = true;
         }
 
+        float* rb = red + (size_t)(red_count & 1) * QMV_ROWS * TOKA;
+        if constexpr (!CC) {
         float acc[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
@@ -371,7 +424,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
             const uint8_t* xst = xfrag + ((st * SG * WPL) * TOKA * 4 + gq * 4 + c) * FB;
 #pragma unroll
             for (int gi = 0; gi < SG; gi++) {
-              if (gi < ng && QMV_PROBE != 1) {
+              if (gi < ng) {
                 const int gl = st * SG + gi;
                 uint32_t wv0[WPL], wv1[WPL];
 #pragma unroll
@@ -461,17 +514,124 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
             }
           }
         } else {
-          float* rb = red + (size_t)(red_count & 1) * QMV_ROWS * TOKA;
 #pragma unroll
           for (int t = 0; t < NT; t++) {
             const int ta = t * 8 + 2 * c;
             if (ta < TOKA) { rb[r0 * TOKA + ta] = acc[t][0]; rb[r1 * TOKA + ta] = acc[t][2]; }
             if (ta + 1 < TOKA) { rb[r0 * TOKA + ta + 1] = acc[t][1]; rb[r1 * TOKA + ta + 1] = acc[t][3]; }
           }
+        }
+        } else {
+          // ---------- CUDA-core consumer (4-bit, <= 4 tokens) ----------
+          // lane = (rs, kc): 16-byte chunk kc of each stage row, rows rs + 4j of the warp's 16
+          const int rs = lane >> 3, kc = lane & 7;
+          float res[4][CC ? NT : 1];
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int t = 0; t < NT; t++) res[j][t] = 0.f;
+          if (!I.zero_rows) {
+            for (int st = 0; st < nst; st++, it_stage++) {
+              const int slot = it_stage % QMV_STAGES;
+              ok &= mbar_wait(&full[slot], (it_stage / QMV_STAGES) & 1);
+              const int ng = (nG - st * SG) < SG ? (nG - st * SG) : SG;
+              if (kc < ng * CPG) {
+                const int ci = st * CPS + kc;  // chunk index within the slice
+                const int gl = ci / CPG;
+                const uint8_t* stg = ring + (size_t)slot * QMV_ROWS * 128;
+                uint4 wv[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                  const int row = warp * 16 + rs + 4 * j;
+                  wv[j] = *reinterpret_cast<const uint4*>(stg + row * 128 + ((kc ^ (row & 7)) << 4));
+                }
+                unsigned long long sacc[4][NT];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+#pragma unroll
+                  for (int t = 0; t < NT; t++) sacc[j][t] = 0ull;
+                const float* xc = xfrag_f + (size_t)ci * XST;
+#pragma unroll
+                for (int wi = 0; wi < 4; wi++) {
+                  // x pairs (x[8wi+2i], x[8wi+2i+1]) for each token
+                  unsigned long long xp[NT][4];
+#pragma unroll
+                  for (int t = 0; t < NT; t++) {
+                    const float4 xa = *reinterpret_cast<const float4*>(xc + t * 32 + wi * 8);
+                    const float4 xb = *reinterpret_cast<const float4*>(xc + t * 32 + wi * 8 + 4);
+                    xp[t][0] = pack_f2(xa.x, xa.y);
+                    xp[t][1] = pack_f2(xa.z, xa.w);
+                    xp[t][2] = pack_f2(xb.x, xb.y);
+                    xp[t][3] = pack_f2(xb.z, xb.w);
+                  }
+#pragma unroll
+                  for (int j = 0; j < 4; j++) {
+                    const uint32_t w = wi == 0 ? wv[j].x : wi == 1 ? wv[j].y : wi == 2 ? wv[j].z : wv[j].w;
+                    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                      // (128 + q) as exact fp32: bytes [0, 0, q, 0x43]
+                      const uint32_t fl = prmt(lo, 0x43000000u, 0x7044u | (i << 8));
+                      const uint32_t fh = prmt(hi, 0x43000000u, 0x7044u | (i << 8));
+                      const unsigned long long wp = pack_u2(fl, fh);  // nibbles (2i, 2i+1)
+#pragma unroll
+                      for (int t = 0; t < NT; t++) ffma2(sacc[j][t], wp, xp[t][i]);
+                    }
+                  }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                  const int row = warp * 16 + rs + 4 * j;
+                  const float sv = __bfloat162float(sbase[row * WS + soff + gl]);
+                  const float bv = fmaf(-128.f, sv, __bfloat162float(sbase[(QMV_ROWS + row) * WS + soff + gl]));
+#pragma unroll
+                  for (int t = 0; t < NT; t++) {
+                    const float2 sp = unpack_f2(sacc[j][t]);
+                    res[j][t] = fmaf(sv, sp.x + sp.y, fmaf(bv, xsum[ci * TOKA + t], res[j][t]));
+                  }
+                }
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[slot]);
+            }
+          }
+          // sum the 8 chunk lanes of each row group
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+              float v = res[j][t];
+              v += __shfl_xor_sync(0xffffffffu, v, 1);
+              v += __shfl_xor_sync(0xffffffffu, v, 2);
+              v += __shfl_xor_sync(0xffffffffu, v, 4);
+              res[j][t] = v;
+            }
+          if (kc == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              const int r = warp * 16 + rs + 4 * j;
+#pragma unroll
+              for (int t = 0; t < NT; t++) {
+                if (t >= TOKA) continue;
+                if (C == 1) {
+                  if (t < ntok && I.n0 + r < p.N) {
+                    const bf16* xr_unused;
+                    bf16* yr;
+                    token_rows(p, mode, I.base, chunk + t, xr_unused, yr);
+                    yr[I.n0 + r] = __float2bfloat16_rn(res[j][t]);
+                  }
+                } else {
+                  rb[r * TOKA + t] = res[j][t];
+                }
+              }
+            }
+          }
+        }
+        if (C > 1) {
           cluster_arrive();
           cluster_wait();
           cg::cluster_group cluster = cg::this_cluster();
-          for (int i = tid; QMV_PROBE != 2 && i < (crow_hi - crow_lo) * ntok; i += 32 * QMV_CWARPS) {
+          for (int i = tid; i < (crow_hi - crow_lo) * ntok; i += 32 * QMV_CWARPS) {
             const int r = crow_lo + i / ntok, tok = i % ntok;
             float s = 0.f;
             for (int q = 0; q < C; q++) s += cluster.map_shared_rank(rb, q)[r * TOKA + tok];
@@ -509,11 +669,11 @@ int sm_count() {
   return n;
 }
 
-template <int BITS, int GS, int NT>
+template <int BITS, int GS, int NT, bool CC>
 static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
-  auto kern = qmv_kernel<BITS, GS, NT>;
+  auto kern = qmv_kernel<BITS, GS, NT, CC>;
   QmvPlan L;
-  L.init(BITS, GS, ks, toka);
+  L.init(BITS, GS, ks, toka, CC);
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -577,9 +737,12 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
   constexpr int SG = QT<BITS, GS>::SG;
   const int64_t KG = a.K / GS;
   const int64_t items = ((a.N + QMV_ROWS - 1) / QMV_ROWS) * zcount;
+  // 4-bit with <= 4 token rows: the CUDA-core consumer (fewer instructions per
+  // weight than an m16n8 MMA that would be 7/8 empty)
+  const bool cc = BITS == 4 && toka <= 4;
   auto smem_of = [&](int ks_, int toka_) {
     QmvPlan L;
-    L.init(BITS, GS, ks_, toka_);
+    L.init(BITS, GS, ks_, toka_, cc);
     return L.total;
   };
   // Pick the cluster size that minimises the busiest cluster's work:
@@ -600,20 +763,28 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     if (cost < best) { best = cost; bestC = C; }
   }
   int C = bestC;
-#ifdef QMV_FORCE_C
-  if (getenv("QMV_FORCE_C")) C = atoi(getenv("QMV_FORCE_C"));
-#endif
+
   int ks = slice_groups(KG, C, SG);
   while (smem_of(ks, toka) > 227 * 1024 && toka > 8) toka -= 8;
   if (smem_of(ks, toka) > 227 * 1024)
     return set_error(VMLX_E_UNSUPPORTED, "qmv: K=%lld too large for the shared-memory plan", (long long)a.K);
   C = (int)((KG + ks - 1) / ks);
+  if constexpr (BITS == 4) {
+    if (cc) {
+      switch (toka) {
+        case 1: return launch_qmv_t<BITS, GS, 1, true>(a, mode, zcount, ks, C, toka, st);
+        case 2: return launch_qmv_t<BITS, GS, 2, true>(a, mode, zcount, ks, C, toka, st);
+        case 3: return launch_qmv_t<BITS, GS, 3, true>(a, mode, zcount, ks, C, toka, st);
+        default: return launch_qmv_t<BITS, GS, 4, true>(a, mode, zcount, ks, C, toka, st);
+      }
+    }
+  }
   const int nt = (toka + 7) / 8;
   switch (nt) {
-    case 1: return launch_qmv_t<BITS, GS, 1>(a, mode, zcount, ks, C, toka, st);
-    case 2: return launch_qmv_t<BITS, GS, 2>(a, mode, zcount, ks, C, toka, st);
-    case 3: return launch_qmv_t<BITS, GS, 3>(a, mode, zcount, ks, C, toka, st);
-    default: return launch_qmv_t<BITS, GS, 4>(a, mode, zcount, ks, C, toka, st);
+    case 1: return launch_qmv_t<BITS, GS, 1, false>(a, mode, zcount, ks, C, toka, st);
+    case 2: return launch_qmv_t<BITS, GS, 2, false>(a, mode, zcount, ks, C, toka, st);
+    case 3: return launch_qmv_t<BITS, GS, 3, false>(a, mode, zcount, ks, C, toka, st);
+    default: return launch_qmv_t<BITS, GS, 4, false>(a, mode, zcount, ks, C, toka, st);
   }
 }
 
