@@ -756,10 +756,13 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     const size_t sm = smem_of(ks, toka);
     if (sm > 227 * 1024) continue;
     int per_sm = (int)((228 * 1024) / (sm + 1024));
-    per_sm = per_sm > 3 ? 3 : (per_sm < 1 ? 1 : per_sm);  // 160 threads x ~128 registers
+    const int reg_cap = cc ? 2 : 3;  // 160 threads x ~150 (CUDA-core) / ~128 (MMA) registers
+    per_sm = per_sm > reg_cap ? reg_cap : (per_sm < 1 ? 1 : per_sm);
     const int64_t clusters = (int64_t)sm_count() * per_sm / C;
     if (clusters < 1) continue;
-    const double cost = (double)((items + clusters - 1) / clusters) * ks + 0.25 * C;
+    // each item also pays a fixed cost (x / scale staging, pipeline fill, the
+    // cluster reduction) worth roughly 8 groups of streaming
+    const double cost = (double)((items + clusters - 1) / clusters) * (ks + 8.0) + 0.5 * C;
     if (cost < best) { best = cost; bestC = C; }
   }
   int C = bestC;
