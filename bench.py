@@ -244,6 +244,133 @@ def cpu_baseline_gemv(M, N, K, bits, gs, seconds=10.0):
 
 
 # ---------------------------------------------------------------------------
+# decode workload
+# ---------------------------------------------------------------------------
+
+def decode_step_bytes(dec, pos):
+    """Algorithmic HBM bytes of one decode step on this rank: every quantized
+    weight once, the KV cache read (pos+1 positions) and the new K/V written."""
+    cfg = dec.cfg
+    kv_read = cfg.n_layers * dec.B * dec.hkv * (pos + 1) * cfg.head_dim * 2 * 2
+    return dec.weight_bytes + kv_read
+
+
+def bench_decode(args, torch, vm, dev, rank, world, all_sum=None):
+    hbm, tf, tf_s, peak_src = peaks()
+    cfg = vm.llama.LlamaConfig(n_layers=args.layers)
+    B, ctx = args.batch, args.ctx
+    pos = ctx  # the step appends token ctx+1 after `ctx` random cached tokens
+    vm.lib().vmlx_set_launch_overlap(1)
+    dec = vm.llama.LlamaDecoder(cfg, B, max_len=ctx + 8, dev=dev, seed=0, rank=rank, world=world,
+                                all_sum=all_sum, cache_fill=ctx)
+    stream = torch.cuda.Stream(dev)
+    x0 = torch.randn(B, cfg.hidden, device=dev, generator=torch.Generator(device=dev).manual_seed(3)).bfloat16()
+    x = x0.clone()
+    g = dec.capture(x, pos, stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        stream.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        with ClockSampler(dev.index or 0) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    t_step = e0.elapsed_time(e1) / 1e3 / args.steps
+    if world > 1:
+        t = torch.tensor([t_step], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_step = t.item()
+    nbytes = decode_step_bytes(dec, pos)
+
+    # dominant kernel: the quantized GEMV; time the step's GEMVs alone (same weights, same graph style)
+    gemv_calls = []
+    for L in dec.layers:
+        gemv_calls += [lambda L=L: L.qkv(dec.h, out=dec.qkv_buf), lambda L=L: L.o(dec.attn.view(B, -1), out=dec.proj),
+                       lambda L=L: L.gate_up(dec.h, out=dec.gu), lambda L=L: L.down(dec.act, out=dec.proj)]
+    t_gemv = time_graph_calls(torch, gemv_calls, 5, 3, stream)
+    gemv_bytes_avg = (dec.weight_bytes + len(gemv_calls) * B * 2 * (cfg.hidden + dec.ffn)) / len(gemv_calls)
+    gemv_achieved = gemv_bytes_avg / t_gemv / 1e9
+
+    # end to end through the public API: host token state in, host state out, every step
+    xh = x0.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    n_e2e = max(8, args.steps // 2)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(n_e2e):
+            dec.decode(xh, out=yh)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = e0.elapsed_time(e1) / 1e3 / n_e2e
+    res = {
+        "metric": "decode tokens/s (Llama-3-8B-shaped decoder, 4-bit g64, TP=N)",
+        "value": round(B / t_step, 2), "unit": "tokens/s", "higher_is_better": True,
+        "ms_per_step": t_step * 1e3, "dtype": "bf16",
+        "config": {"workload": f"BASELINE config 3: {cfg.n_layers} Llama-3-8B-shaped blocks (hidden 4096, "
+                               f"32 Q / 8 KV heads, hd 128, FFN 14336, 4-bit g64), batch {B}, bf16 KV cache of "
+                               f"{ctx} random tokens, TP={world}",
+                   "batch": B, "context": ctx, "layers": cfg.n_layers, "parallelism": f"tp{world}",
+                   "l2": f"inputs larger than L2: {nbytes / 1e9:.2f} GB of weights + KV per step per rank",
+                   "graph": "whole decode step captured in one CUDA graph", "launch_overlap": "on"},
+        "step_hbm": {"bytes_per_rank": nbytes, "GBps_per_rank": round(nbytes / t_step / 1e9, 1),
+                     "frac_of_measured": round(nbytes / t_step / 1e9 / hbm, 4)},
+        "roofline": {"bound": "hbm", "kernel": "qmv_kernel (decode GEMV)", "achieved": round(gemv_achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gemv_achieved / hbm, 4), "peak_source": peak_src,
+                     "frac_of_8TBps": round(gemv_achieved / 8000, 4),
+                     "traffic": load_traffic(f"qmv_decode_B{B}"),
+                     "algorithmic_bytes_per_launch": int(gemv_bytes_avg), "us_per_launch": round(t_gemv * 1e6, 2)},
+        "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
+                "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2},
+        "gpu_launches": args.steps * dec.launches_per_step,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_baseline_decode(B, ctx, cfg, seconds=args.cpu_seconds)
+    return res
+
+
+def cpu_baseline_decode(B, ctx, cfg, seconds=10.0):
+    """CPU restatement of one decode step (oracle GEMVs of one layer + numpy
+    attention over the cache), timed over whole layers and scaled to the stack."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    rng = np.random.default_rng(0)
+    H, D, Hq, Hkv, F = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.ffn
+
+    def qw(n, k):
+        return oracle.quantize(oracle.f32_to_bf16(rng.normal(0, 0.02, (n, k)).astype(np.float32)), 64, 4)
+    mats = [((Hq + 2 * Hkv) * D, H), (H, Hq * D), (2 * F, H), (H, F)]
+    ws = [qw(n, k) for n, k in mats]
+    kc = rng.normal(size=(B, Hkv, ctx + 1, D)).astype(np.float32)
+    vc = rng.normal(size=(B, Hkv, ctx + 1, D)).astype(np.float32)
+    xs = [oracle.f32_to_bf16(rng.normal(size=(B, k)).astype(np.float32)) for _, k in mats]
+    q = rng.normal(size=(B, Hq, D)).astype(np.float32)
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n == 0:
+        for (wq, s, b), x in zip(ws, xs):
+            oracle.qmm_fp32_bf16(x, wq, s, b, 64, 4)
+        G = Hq // Hkv
+        sc = np.einsum("bhgd,bhtd->bhgt", q.reshape(B, Hkv, G, D), kc) * D ** -0.5
+        p = np.exp(sc - sc.max(-1, keepdims=True))
+        np.einsum("bhgt,bhtd->bhgd", p / p.sum(-1, keepdims=True), vc)
+        n += 1
+    dt_layer = (time.perf_counter() - t0) / n
+    t_tok = dt_layer * cfg.n_layers
+    return {"value": round(B / t_tok, 4), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{n} layer steps (4 quantized GEMVs via the OpenMP C restatement + numpy attention over "
+                      f"{ctx + 1} cached tokens) in {seconds:.0f} s, scaled to {cfg.n_layers} layers",
+            "ms_per_token": round(t_tok * 1e3, 2)}
+
+
+# ---------------------------------------------------------------------------
 # driver
 # ---------------------------------------------------------------------------
 
@@ -253,11 +380,14 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default=os.environ.get("VMLX_BENCH_WORKLOAD", "gemv"),
+    ap.add_argument("--workload", default=os.environ.get("VMLX_BENCH_WORKLOAD", "decode"),
                     choices=["gemv", "decode"])
     ap.add_argument("--quick", action="store_true", help="skip the config-2 sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=1, help="decode batch (config 3: 1, 16, 64)")
+    ap.add_argument("--ctx", type=int, default=4096, help="cached tokens before the step")
+    ap.add_argument("--layers", type=int, default=32, help="decoder blocks (Llama-3-8B has 32)")
     args = ap.parse_args()
     rank, world, local = dist_env()
 
@@ -292,21 +422,44 @@ def main():
         if rank == 0:
             print(json.dumps(res), flush=True)
     else:
-        raise SystemExit("decode workload not built yet")
+        all_sum = None
+        if world > 1:
+            raise SystemExit("tensor-parallel decode: see vmlx_b200.distributed")
+        res = bench_decode(args, torch, vm, dev, rank, world, all_sum)
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
+                    "vs_baseline": None, "data": "synthetic (seeded random weights, tokens and KV cache)"})
+        if rank == 0:
+            print(json.dumps(res), flush=True)
 
 
 def reference_arm(args, world):
+    """The reference's own CPU path for this workload (MLX's CPU code is absent
+    from the reference checkout, so: the C restatement of its arithmetic)."""
+    note = ("reference CPU path = C restatement of MLX's affine qmv (MLX's own CPU code is absent from the "
+            "reference checkout)")
+    if args.workload == "decode":
+        sys.path.insert(0, ROOT)
+        from vmlx_b200_loader import load_package
+        vm = load_package()
+        cfg = vm.llama.LlamaConfig(n_layers=args.layers)
+        cpu = cpu_baseline_decode(args.batch, args.ctx, cfg, seconds=args.cpu_seconds)
+        return {"impl": "reference", "metric": "decode tokens/s (Llama-3-8B-shaped decoder, 4-bit g64, TP=N)",
+                "value": cpu["value"], "unit": "tokens/s", "higher_is_better": True, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["ms_per_token"], "dtype": "bf16",
+                "data": "synthetic (seeded numpy PCG64)", "scaling": "strong", "vs_baseline": None,
+                "config": {"workload": f"BASELINE config 3: {cfg.n_layers} Llama-3-8B-shaped blocks, batch "
+                                       f"{args.batch}, {args.ctx} cached tokens", "batch": args.batch,
+                           "context": args.ctx, "layers": cfg.n_layers, "note": note},
+                "cpu_baseline": cpu,
+                "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     M, N, K, bits, gs = 1, 4096, 4096, 4, 64
-    per_step = max(1.0, 60.0 / max(1, args.steps + args.warmup))
-    cpu = cpu_baseline_gemv(M, N, K, bits, gs, seconds=min(args.cpu_seconds, per_step * args.steps))
+    cpu = cpu_baseline_gemv(M, N, K, bits, gs, seconds=args.cpu_seconds)
     return {"impl": "reference", "metric": "quantized GEMV HBM GB/s (4096x4096, 4-bit g64, M=1)",
             "value": cpu["value"], "unit": "GB/s", "higher_is_better": True, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["us_per_call"] / 1e3,
             "dtype": "bf16", "data": "synthetic (seeded numpy PCG64)", "scaling": "weak", "vs_baseline": None,
             "config": {"workload": "BASELINE config 1: MLX affine quantized_matmul GEMV", "M": M, "N": N, "K": K,
-                       "bits": bits, "group_size": gs,
-                       "note": "reference CPU path = C restatement of MLX's affine qmv (MLX's own CPU "
-                               "code is absent from the reference checkout)"},
+                       "bits": bits, "group_size": gs, "note": note},
             "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 

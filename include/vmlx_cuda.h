@@ -131,6 +131,59 @@ VMLX_API int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, con
                          const char* mode, bool sorted_indices, int64_t batch, int64_t x_batches,
                          int64_t M, int64_t N, int64_t K, int64_t n_experts, void* stream);
 
+
+/* ---- decoder-block support kernels (bf16) ---- */
+
+/*
+ * out[r, :] = weight * bf16(x[r, :] * rsqrt(mean(x[r, :]^2) + eps)), fp32 sums.
+ * Replaces MLXFast.rmsNorm (Source/MLX/MLXFast.swift:230; kernel
+ * mlx-generated/metal/rms_norm.metal:13-81).  dims a multiple of 8.
+ */
+VMLX_API int vmlx_cuda_rms_norm(void* out, const void* x, const void* weight, float eps, int64_t rows,
+                                int64_t dims, void* stream);
+
+/*
+ * Decode-step RoPE + KV-cache append for a fused qkv projection.
+ *   qkv     bf16 [batch, (n_heads + 2*n_kv_heads) * head_dim]   (q | k | v)
+ *   q_out   bf16 [batch, n_heads, head_dim]   rotated q
+ *   k_cache, v_cache bf16 [batch, n_kv_heads, max_len, head_dim]; the rotated
+ *           k and the v of this step are written at position `pos`.
+ * Non-traditional rotation of pairs (i, i + head_dim/2) by
+ * theta = scale * pos * base^(-2i/head_dim) (mlx-generated/metal/rope.metal:55-229,
+ * Libraries/MLXLLM/Models/Llama.swift:66-67; KVCacheSimple.update,
+ * Libraries/MLXLMCommon/KVCache.swift:452-470).
+ */
+VMLX_API int vmlx_cuda_rope_qkv(void* q_out, void* k_cache, void* v_cache, const void* qkv, int64_t batch,
+                                int n_heads, int n_kv_heads, int head_dim, int64_t pos, int64_t max_len,
+                                float base, float scale, void* stream);
+
+/* Bytes of workspace vmlx_cuda_sdpa_decode needs for these sizes. */
+VMLX_API size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int64_t kv_len, int head_dim);
+
+/*
+ * Decode attention (one query token per sequence) over a bf16 KV cache:
+ *   out[b, h, :] = softmax(scale * q[b, h] . K[b, h/G, :kv_len]^T) V[b, h/G, :kv_len]
+ * q bf16 [batch, n_heads, 128]; caches as for vmlx_cuda_rope_qkv; G =
+ * n_heads / n_kv_heads in 1..8 (grouped-query attention).  fp32 softmax and
+ * accumulation.  The cache is split over CTAs; `workspace` (caller-owned,
+ * vmlx_cuda_sdpa_decode_workspace bytes) holds the per-split partials.
+ * Replaces MLXFast.scaledDotProductAttention for decode
+ * (Source/MLX/MLXFast.swift:118; kernels mlx-generated/metal/sdpa_vector.h:15-394).
+ */
+VMLX_API int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                   int64_t batch, int n_heads, int n_kv_heads, int head_dim, int64_t kv_len,
+                                   int64_t max_len, float scale, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/*
+ * out[r, j] = bf16(bf16(silu(g)) * u) with gate_up bf16 [rows, 2*ffn] = g | u
+ * (compiledSwiGLU, Libraries/MLXLMCommon/SwitchLayers.swift:40-50).
+ */
+VMLX_API int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, int64_t ffn, void* stream);
+
+/* out = bf16(a + b), n elements (the residual adds of a decoder block). */
+VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

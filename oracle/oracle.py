@@ -215,3 +215,41 @@ def moe_route(logits: np.ndarray, k: int, norm_topk_prob: bool = False):
     if norm_topk_prob:
         sc = sc / sc.sum(-1, keepdims=True)
     return top.astype(np.uint32), sc
+
+
+# ---- decoder-block references (numpy, fp64 math with the reference's bf16 rounding points) ----
+
+def rms_norm_ref(x_bf16, w_bf16, eps):
+    """MLXFast.rmsNorm: w * bf16(x * rsqrt(mean(x^2) + eps)) -> bf16 floats."""
+    x = bf16_to_f32(x_bf16).astype(np.float64)
+    w = bf16_to_f32(w_bf16).astype(np.float64)
+    inv = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    n = round_bf16((x * inv).astype(np.float32)).astype(np.float64)
+    return round_bf16((w * n).astype(np.float32))
+
+
+def rope_ref(x, pos, base, scale=1.0):
+    """Non-traditional RoPE of x [..., D] (float) at position pos."""
+    D = x.shape[-1]
+    half = D // 2
+    d = np.arange(half, dtype=np.float64)
+    inv_freq = base ** (-d / half)
+    th = scale * pos * inv_freq
+    c, s = np.cos(th), np.sin(th)
+    x1, x2 = x[..., :half].astype(np.float64), x[..., half:].astype(np.float64)
+    return np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], -1)
+
+
+def sdpa_ref(q, k, v, scale):
+    """q [B, Hq, D]; k, v [B, Hkv, L, D] (floats) -> [B, Hq, D] fp64 (GQA)."""
+    B, Hq, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    out = np.zeros((B, Hq, D))
+    for b in range(B):
+        for h in range(Hq):
+            kk, vv = k[b, h // G].astype(np.float64), v[b, h // G].astype(np.float64)
+            s = kk @ q[b, h].astype(np.float64) * scale
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ vv
+    return out

@@ -10,3 +10,4 @@ from . import ops, nn, switch_layers  # noqa: F401
 from .ops import dequantized, gather_quantized_mm, quantized, quantized_mm  # noqa: F401
 from .nn import QuantizedLinear  # noqa: F401
 from .switch_layers import QuantizedSwitchLinear, SwitchGLU, gather_sort, scatter_unsort  # noqa: F401
+from . import fast, llama  # noqa: F401,E402
