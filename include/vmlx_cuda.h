@@ -176,6 +176,24 @@ VMLX_API int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache
                                    void* stream);
 
 /*
+ * Allocation-free variant of vmlx_cuda_sdpa_decode, for callers that cannot
+ * allocate device memory where they run attention (a fixed memory pool owned
+ * by the engine, a host that forbids allocation on its inference thread, or
+ * code that must not risk a cudaMalloc mid-decode).  The per-split partials
+ * live in an 8 MiB array inside the library's device image (held on every GPU
+ * that loads the library until the process exits); calls needing more
+ * (batch * n_heads * min(64, ceil(kv_len/256)) * (head_dim + 2) * 4 bytes) are
+ * rejected with VMLX_E_INVALID.  The first call on a device looks up the
+ * array's address with that device current, so make it before any stream
+ * capture.  All calls on a device share the array: calls that may overlap on
+ * the GPU race.  Nothing needs clearing between calls.  No counterpart in the
+ * reference.
+ */
+VMLX_API int vmlx_cuda_sdpa_decode_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                           int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                           int64_t kv_len, int64_t max_len, float scale, void* stream);
+
+/*
  * out[r, j] = bf16(bf16(silu(g)) * u) with gate_up bf16 [rows, 2*ffn] = g | u
  * (compiledSwiGLU, Libraries/MLXLMCommon/SwitchLayers.swift:40-50).
  */

@@ -51,6 +51,8 @@ SIGNATURES = {
     "vmlx_cuda_sdpa_decode_workspace": (_sz, [_i64, _int, _i64, _int]),
     "vmlx_cuda_sdpa_decode": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _c.c_float, _vp,
                                      _sz, _vp]),
+    "vmlx_cuda_sdpa_decode_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64,
+                                             _c.c_float, _vp]),
     "vmlx_cuda_silu_mul": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
 }

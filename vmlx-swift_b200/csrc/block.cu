@@ -14,6 +14,8 @@
 #include "kernels.cuh"
 #include "sm100_util.cuh"
 
+#include <mutex>
+
 namespace vmlx {
 
 // ---------------------------------------------------------------- RMSNorm --
@@ -375,4 +377,89 @@ extern "C" int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n,
   if (n <= 0) return n == 0 ? VMLX_OK : set_error(VMLX_E_INVALID, "add: bad size");
   add_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>((const bf16*)a, (const bf16*)b, (bf16*)out, n);
   return check_launch("vmlx_cuda_add");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: an engine that hands the library only the buffers it already owns
+// (a fixed memory pool reserved at start-up, a plug-in host that forbids
+// allocation on its inference thread, code that must not call cudaMalloc
+// because that call can synchronise the device or fail under memory pressure
+// mid-decode).  For them this entry point keeps the per-split partials in a
+// fixed array that lives inside the library's device image, so the call needs
+// nothing but its inputs and output.
+//
+// Limits and behaviour:
+//  * the array holds SDPA_NOALLOC_BYTES (8 MiB) per GPU, for as long as the
+//    process has the library loaded on that GPU; calls whose partials need
+//    more (batch * n_heads * ceil(kv_len/256, at most 64) * (head_dim + 2) * 4
+//    bytes) are rejected with VMLX_E_INVALID;
+//  * the first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress) with that device current; make that first call
+//    before any stream capture;
+//  * every call on a device shares the one array: calls that can overlap on
+//    the GPU (different streams without ordering) race and must not be issued;
+//  * each call writes every partial it later reads, so nothing needs clearing
+//    and stale contents of an earlier call are never used.
+// ---------------------------------------------------------------------------
+constexpr size_t SDPA_NOALLOC_BYTES = (size_t)8 << 20;
+static __device__ __align__(256) float g_sdpa_noalloc_scratch[SDPA_NOALLOC_BYTES / sizeof(float)];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array on the current device (set up once per device).
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "sdpa_decode_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_sdpa_noalloc_scratch), "sdpa_decode_noalloc: cudaGetSymbolAddress");
+    if (rc) return rc;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_cuda_sdpa_decode_noalloc(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                             int64_t batch, int n_heads, int n_kv_heads, int head_dim, int64_t kv_len,
+                                             int64_t max_len, float scale, void* stream) {
+  if (!out || !q || !k_cache || !v_cache) return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: null pointer");
+  if (head_dim != SDPA_D)
+    return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode_noalloc: head_dim=%d (only 128)", head_dim);
+  if (n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
+    return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode_noalloc: %d q heads per kv head (1..8 supported)",
+                     n_kv_heads > 0 ? n_heads / n_kv_heads : 0);
+  if (kv_len <= 0 || kv_len > max_len || batch < 0)
+    return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: kv_len=%lld", (long long)kv_len);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16))
+    return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: pointers must be 16-byte aligned");
+  const size_t need = vmlx_cuda_sdpa_decode_workspace(batch, n_heads, kv_len, head_dim);
+  if (need > SDPA_NOALLOC_BYTES)
+    return set_error(VMLX_E_INVALID,
+                     "sdpa_decode_noalloc: these sizes need %zu bytes of partials, more than the %zu-byte "
+                     "built-in scratch; use vmlx_cuda_sdpa_decode with a workspace",
+                     need, SDPA_NOALLOC_BYTES);
+  if (batch == 0) return VMLX_OK;
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  const int splits = sdpa_splits(kv_len);
+  const int chunk = (int)((kv_len + splits - 1) / splits);
+  const int G = n_heads / n_kv_heads;
+  cudaStream_t st = as_stream(stream);
+  dim3 grid((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
+  sdpa_decode_kernel<<<grid, 32 * G, 0, st>>>((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache,
+                                             (float*)scratch, n_heads, n_kv_heads, (int)kv_len, (int)max_len, chunk,
+                                             scale * 1.4426950408889634f);
+  rc = check_launch("sdpa_decode_kernel (noalloc)");
+  if (rc) return rc;
+  sdpa_combine_kernel<<<(unsigned)(batch * n_heads), SDPA_D, 0, st>>>((const float*)scratch, (bf16*)out, splits);
+  return check_launch("sdpa_combine_kernel (noalloc)");
 }
