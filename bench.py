@@ -422,10 +422,14 @@ def main():
         if rank == 0:
             print(json.dumps(res), flush=True)
     else:
-        all_sum = None
+        all_sum, grp = None, None
         if world > 1:
-            raise SystemExit("tensor-parallel decode: see vmlx_b200.distributed")
+            # one rank per GPU: P2P all-reduce group bootstrapped over torch.distributed (NCCL only for the bootstrap)
+            grp = vm.distributed.Group(strict=True)
+            all_sum = grp.all_sum
         res = bench_decode(args, torch, vm, dev, rank, world, all_sum)
+        if grp is not None:
+            res["tp_status"] = grp.status()
         res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
                     "vs_baseline": None, "data": "synthetic (seeded random weights, tokens and KV cache)"})
         if rank == 0:

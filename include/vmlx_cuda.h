@@ -202,6 +202,50 @@ VMLX_API int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, in
 /* out = bf16(a + b), n elements (the residual adds of a decoder block). */
 VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream);
 
+/* ---- tensor parallelism (one rank per GPU) ---- */
+
+/*
+ * A tensor-parallel group member on the current device: the counterpart of
+ * vmlx_group_init / vmlx_group_rank / vmlx_group_size
+ * (Libraries/CmlxDistributedShim/include/CmlxDistributedShim.h:21-42) for
+ * one rank.  Allocates this rank's receive buffer (2 x world x max_bytes
+ * slots plus flags); max_bytes bounds the bytes of one all-reduce (multiple
+ * of 16).  The handle owns the buffer; vmlx_tp_destroy frees it.
+ * Bootstrap: every rank exports vmlx_tp_ipc_handle (64 bytes, a CUDA IPC
+ * handle), the handles are exchanged out of band (the Python Group uses
+ * torch.distributed), and every rank calls vmlx_tp_open_peers with the
+ * world's handles in rank order.  A process driving several GPUs can instead
+ * pass peer buffers (vmlx_tp_buffer of the other handles) to vmlx_tp_set_peer.
+ */
+VMLX_API int vmlx_tp_create(int rank, int world, size_t max_bytes, void** out);
+VMLX_API int vmlx_tp_rank(void* tp);
+VMLX_API int vmlx_tp_size(void* tp);
+VMLX_API int vmlx_tp_ipc_handle(void* tp, void* handle_out);
+VMLX_API int vmlx_tp_open_peers(void* tp, const void* handles);
+VMLX_API int vmlx_tp_set_peer(void* tp, int peer, void* device_ptr);
+VMLX_API void* vmlx_tp_buffer(void* tp);
+/* Bound of every wait on a peer (default 2 s); after it the call gives up. */
+VMLX_API int vmlx_tp_set_timeout_us(void* tp, uint64_t us);
+
+/*
+ * out = sum over the group's ranks of `in` (n bf16 elements, n*2 <= max_bytes,
+ * 16-byte aligned), identical bits on every rank (fixed rank order, fp32
+ * sums).  Replaces vmlx_all_sum (Libraries/CmlxDistributedShim/CmlxDistributedShim.c:54-60)
+ * behind Collectives.allSum (Libraries/MLXDistributedTP/Collectives.swift:27-32).
+ * One kernel: P2P stores of this rank's data into every rank's buffer, flags
+ * with release/acquire at system scope, bounded waits.  Every rank must make
+ * the same sequence of calls.  Size 1: a copy.  Stream ordered; graph-capturable.
+ */
+VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, void* stream);
+
+/*
+ * Reads (synchronously) and clears the group's device status word:
+ * *code = 0, or VMLX_E_PEER_TIMEOUT if some wait on a peer ran out since the
+ * last read.
+ */
+VMLX_API int vmlx_tp_status(void* tp, int* code);
+VMLX_API int vmlx_tp_destroy(void* tp);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,3 +11,4 @@ from .ops import dequantized, gather_quantized_mm, quantized, quantized_mm  # no
 from .nn import QuantizedLinear  # noqa: F401
 from .switch_layers import QuantizedSwitchLinear, SwitchGLU, gather_sort, scatter_unsort  # noqa: F401
 from . import fast, llama  # noqa: F401,E402
+from . import distributed  # noqa: F401,E402

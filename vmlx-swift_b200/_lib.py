@@ -55,6 +55,17 @@ SIGNATURES = {
                                              _c.c_float, _vp]),
     "vmlx_cuda_silu_mul": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "vmlx_tp_create": (_int, [_int, _int, _sz, _c.POINTER(_vp)]),
+    "vmlx_tp_rank": (_int, [_vp]),
+    "vmlx_tp_size": (_int, [_vp]),
+    "vmlx_tp_ipc_handle": (_int, [_vp, _vp]),
+    "vmlx_tp_open_peers": (_int, [_vp, _vp]),
+    "vmlx_tp_set_peer": (_int, [_vp, _int, _vp]),
+    "vmlx_tp_buffer": (_vp, [_vp]),
+    "vmlx_tp_set_timeout_us": (_int, [_vp, _c.c_uint64]),
+    "vmlx_tp_all_sum": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "vmlx_tp_status": (_int, [_vp, _c.POINTER(_int)]),
+    "vmlx_tp_destroy": (_int, [_vp]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,290 @@
+// tp.cu -- tensor-parallel group handle and the one-shot all-reduce over NVLink P2P.
+//
+// Replaces the reference's collective path for row-parallel linears:
+//   ShardedToAllLinear.callAsFunction (Libraries/MLXDistributedTP/LinearLayers.swift:198-205)
+//   -> Collectives.allSum (Collectives.swift:27-32) -> vmlx_all_sum
+//   (Libraries/CmlxDistributedShim/CmlxDistributedShim.c:54-60) -> mlx distributed::all_sum.
+//
+// Design (one process per GPU, or one process driving several GPUs):
+//  * Every rank owns one device buffer: [2 parities][world][max_bytes] receive
+//    slots, then [2][world][TP_MAX_CTAS] uint32 flags, then [TP_MAX_CTAS] epochs.
+//    Peers map it with CUDA IPC (or get its pointer directly in one process).
+//  * all_sum is one kernel: CTA c takes chunk c of the vector, stores it into
+//    slot [parity][my_rank] of every rank's buffer (P2P stores over NVLink /
+//    NVSwitch, including itself), fences at system scope, publishes flag
+//    [parity][my_rank][c] = epoch on every rank (st.release.sys), waits for
+//    the world's flags in its own buffer (ld.acquire.sys, bounded by a
+//    globaltimer deadline), then sums the world slots in fixed rank order
+//    (identical result on every rank) and writes the output.
+//  * The epoch of chunk c lives in device memory and is advanced by the kernel,
+//    so a captured CUDA graph can be replayed; flags are monotonic, no resets.
+//    Two parities of slots let a rank run one call ahead of a slow peer
+//    without overwriting data that peer still reads.
+//  * A wait that runs out records VMLX_E_PEER_TIMEOUT in the handle's status
+//    word and returns; the context stays usable (vmlx_tp_status reads it).
+// NCCL is used only as the measured baseline, outside this library.
+#include <cstdlib>
+#include <cstring>
+
+#include "kernels.cuh"
+
+namespace vmlx {
+
+constexpr int TP_MAX_WORLD = 8;
+constexpr int TP_MAX_CTAS = 64;
+constexpr int TP_THREADS = 256;
+
+struct TpPeers {
+  char* buf[TP_MAX_WORLD];  // every rank's buffer base, as seen from this device
+};
+
+struct TpHandle {
+  int rank, world, device;
+  size_t max_bytes;        // bytes per slot
+  char* local;             // this rank's buffer
+  size_t total_bytes;
+  cudaIpcMemHandle_t ipc;
+  bool ipc_valid;
+  char* peer_base[TP_MAX_WORLD];  // mapped buffers (IPC-opened or given)
+  bool peer_opened[TP_MAX_WORLD];
+  int* status;             // device word: 0 or VMLX_E_PEER_TIMEOUT
+  uint64_t timeout_ns;
+  bool connected;
+};
+
+__host__ __device__ inline size_t tp_slot_off(int parity, int src, size_t max_bytes, int world) {
+  return ((size_t)parity * world + src) * max_bytes;
+}
+__host__ __device__ inline size_t tp_flag_off(size_t max_bytes, int world) {
+  return (size_t)2 * world * max_bytes;
+}
+__host__ __device__ inline size_t tp_epoch_off(size_t max_bytes, int world) {
+  return tp_flag_off(max_bytes, world) + (size_t)2 * world * TP_MAX_CTAS * sizeof(uint32_t);
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One-shot all-reduce of n bf16 elements (n * 2 <= max_bytes, chunked over CTAs).
+__global__ void __launch_bounds__(TP_THREADS)
+tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
+                  bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns) {
+  const int c = blockIdx.x;
+  const int64_t e0 = (int64_t)c * chunk;
+  const int64_t e1 = e0 + chunk < n ? e0 + chunk : n;
+  char* mine = peers.buf[rank];
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(mine + tp_epoch_off(max_bytes, world)) + c;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_epoch = *epoch_p + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int parity = e & 1;
+
+  // 1. push my chunk into slot [parity][rank] of every rank (16-byte stores when aligned)
+  const bool vec = ((e0 | e1) & 7) == 0;
+  for (int r = 0; r < world; r++) {
+    bf16* dst = reinterpret_cast<bf16*>(peers.buf[r] + tp_slot_off(parity, rank, max_bytes, world));
+    if (vec) {
+      for (int64_t i = e0 + threadIdx.x * 8; i < e1; i += TP_THREADS * 8)
+        *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(in + i);
+    } else {
+      for (int64_t i = e0 + threadIdx.x; i < e1; i += TP_THREADS) dst[i] = in[i];
+    }
+  }
+  __syncthreads();
+  // 2. publish: flag [parity][rank][c] = e on every rank
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    uint32_t* f = reinterpret_cast<uint32_t*>(peers.buf[threadIdx.x] + tp_flag_off(max_bytes, world)) +
+                  ((size_t)parity * world + rank) * TP_MAX_CTAS + c;
+    st_release_sys(f, e);
+  }
+  // 3. wait for every rank's chunk in my buffer (bounded)
+  if (threadIdx.x < world) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + tp_flag_off(max_bytes, world)) +
+                        ((size_t)parity * world + threadIdx.x) * TP_MAX_CTAS + c;
+    const uint64_t deadline = globaltimer() + timeout_ns;
+    bool arrived = false;
+    for (uint32_t it = 0;; it++) {
+      if ((int32_t)(ld_acquire_sys(f) - e) >= 0) { arrived = true; break; }
+      if ((it & 1023) == 1023 && globaltimer() > deadline) break;
+    }
+    if (!arrived) {
+      s_ok = 0;
+      atomicExch(status, VMLX_E_PEER_TIMEOUT);
+    }
+  }
+  __syncthreads();
+  // 4. reduce in rank order (bitwise identical on every rank)
+  if (s_ok) {
+    for (int64_t i = e0 + threadIdx.x; i < e1; i += TP_THREADS) {
+      float s = 0.f;
+      for (int r = 0; r < world; r++)
+        s += __bfloat162float(reinterpret_cast<const bf16*>(mine + tp_slot_off(parity, r, max_bytes, world))[i]);
+      out[i] = __float2bfloat16_rn(s);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch_p = e;
+}
+
+static int tp_check(TpHandle* h) {
+  if (!h) return set_error(VMLX_E_INVALID, "tp: null handle");
+  return VMLX_OK;
+}
+
+}  // namespace vmlx
+
+using namespace vmlx;
+
+extern "C" int vmlx_tp_create(int rank, int world, size_t max_bytes, void** out) {
+  if (!out) return set_error(VMLX_E_INVALID, "tp_create: null out");
+  if (world < 1 || world > TP_MAX_WORLD || rank < 0 || rank >= world)
+    return set_error(VMLX_E_INVALID, "tp_create: rank %d / world %d (world 1..%d)", rank, world, TP_MAX_WORLD);
+  if (max_bytes == 0 || max_bytes % 16) return set_error(VMLX_E_INVALID, "tp_create: max_bytes must be a positive multiple of 16");
+  TpHandle* h = new TpHandle();
+  std::memset(h, 0, sizeof(*h));
+  h->rank = rank;
+  h->world = world;
+  h->max_bytes = max_bytes;
+  h->timeout_ns = 2000000000ull;  // 2 s
+  int rc = check_cuda(cudaGetDevice(&h->device), "tp_create: cudaGetDevice");
+  h->total_bytes = tp_epoch_off(max_bytes, world) + TP_MAX_CTAS * sizeof(uint32_t);
+  if (!rc) rc = check_cuda(cudaMalloc(&h->local, h->total_bytes), "tp_create: cudaMalloc");
+  if (!rc) rc = check_cuda(cudaMemset(h->local, 0, h->total_bytes), "tp_create: cudaMemset");
+  if (!rc) rc = check_cuda(cudaMalloc(&h->status, sizeof(int)), "tp_create: cudaMalloc status");
+  if (!rc) rc = check_cuda(cudaMemset(h->status, 0, sizeof(int)), "tp_create: cudaMemset status");
+  if (!rc) {
+    h->ipc_valid = cudaIpcGetMemHandle(&h->ipc, h->local) == cudaSuccess;
+    cudaGetLastError();
+  }
+  if (rc) {
+    if (h->local) cudaFree(h->local);
+    if (h->status) cudaFree(h->status);
+    delete h;
+    return rc;
+  }
+  h->peer_base[rank] = h->local;
+  *out = h;
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_rank(void* tp) { return tp ? static_cast<TpHandle*>(tp)->rank : -1; }
+extern "C" int vmlx_tp_size(void* tp) { return tp ? static_cast<TpHandle*>(tp)->world : -1; }
+
+extern "C" int vmlx_tp_ipc_handle(void* tp, void* handle_out) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (!handle_out) return set_error(VMLX_E_INVALID, "tp_ipc_handle: null out");
+  if (!h->ipc_valid) return set_error(VMLX_E_CUDA, "tp_ipc_handle: the buffer has no IPC handle");
+  std::memcpy(handle_out, &h->ipc, sizeof(cudaIpcMemHandle_t));
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_open_peers(void* tp, const void* handles) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (!handles) return set_error(VMLX_E_INVALID, "tp_open_peers: null handles");
+  for (int r = 0; r < h->world; r++) {
+    if (r == h->rank) continue;
+    cudaIpcMemHandle_t ph;
+    std::memcpy(&ph, static_cast<const char*>(handles) + (size_t)r * sizeof(cudaIpcMemHandle_t), sizeof(ph));
+    void* p = nullptr;
+    rc = check_cuda(cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess), "tp_open_peers: cudaIpcOpenMemHandle");
+    if (rc) return rc;
+    h->peer_base[r] = static_cast<char*>(p);
+    h->peer_opened[r] = true;
+  }
+  h->connected = true;
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_set_peer(void* tp, int peer, void* device_ptr) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (peer < 0 || peer >= h->world || peer == h->rank || !device_ptr)
+    return set_error(VMLX_E_INVALID, "tp_set_peer: bad peer %d", peer);
+  h->peer_base[peer] = static_cast<char*>(device_ptr);
+  bool all = true;
+  for (int r = 0; r < h->world; r++) all &= h->peer_base[r] != nullptr;
+  h->connected = all;
+  return VMLX_OK;
+}
+
+extern "C" void* vmlx_tp_buffer(void* tp) { return tp ? static_cast<TpHandle*>(tp)->local : nullptr; }
+
+extern "C" int vmlx_tp_set_timeout_us(void* tp, uint64_t us) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  h->timeout_ns = us * 1000ull;
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, void* stream) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (!out || !in) return set_error(VMLX_E_INVALID, "tp_all_sum: null pointer");
+  if (n < 0 || (size_t)n * 2 > h->max_bytes)
+    return set_error(VMLX_E_INVALID, "tp_all_sum: %lld elements exceed the %zu-byte slots", (long long)n, h->max_bytes);
+  if (n == 0) return VMLX_OK;
+  if (!aligned(out, 16) || !aligned(in, 16)) return set_error(VMLX_E_INVALID, "tp_all_sum: pointers must be 16-byte aligned");
+  if (h->world == 1) {
+    if (out != in) return check_cuda(cudaMemcpyAsync(out, in, (size_t)n * 2, cudaMemcpyDeviceToDevice, as_stream(stream)),
+                                     "tp_all_sum: copy");
+    return VMLX_OK;
+  }
+  if (!h->connected) return set_error(VMLX_E_STATE, "tp_all_sum: peers not connected");
+  // chunks of >= 2048 elements, at most TP_MAX_CTAS CTAs, multiples of 8 elements
+  int64_t ctas = (n + 2047) / 2048;
+  if (ctas > TP_MAX_CTAS) ctas = TP_MAX_CTAS;
+  int64_t chunk = ((n + ctas - 1) / ctas + 7) / 8 * 8;
+  ctas = (n + chunk - 1) / chunk;
+  TpPeers peers;
+  for (int r = 0; r < TP_MAX_WORLD; r++) peers.buf[r] = r < h->world ? h->peer_base[r] : nullptr;
+  tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
+      peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
+  return check_launch("tp_all_sum_kernel");
+}
+
+extern "C" int vmlx_tp_status(void* tp, int* code) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  int v = 0;
+  rc = check_cuda(cudaMemcpy(&v, h->status, sizeof(int), cudaMemcpyDeviceToHost), "tp_status: read");
+  if (rc) return rc;
+  if (code) *code = v;
+  if (v) cudaMemset(h->status, 0, sizeof(int));
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_destroy(void* tp) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  if (!h) return VMLX_OK;
+  for (int r = 0; r < h->world; r++)
+    if (h->peer_opened[r]) cudaIpcCloseMemHandle(h->peer_base[r]);
+  if (h->local) cudaFree(h->local);
+  if (h->status) cudaFree(h->status);
+  delete h;
+  return VMLX_OK;
+}

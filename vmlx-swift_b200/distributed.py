@@ -1,0 +1,141 @@
+"""Tensor parallelism: group, all-reduce and sharded quantized linears.
+
+Mirrors Libraries/MLXDistributedTP:
+  Group(strict:backend:) / .rank / .size            Group.swift:15-65
+  Collectives.allSum                               Collectives.swift:27-32 (identity for size 1, :20-28)
+  AllToShardedLinear / ShardedToAllLinear          LinearLayers.swift:23-206
+  shardLinear / ShardingPlan                       Sharding.swift:24-36, ShardingPlan.swift:55-154
+The reference has no quantized TP ("not here yet", MLXDistributedTP/README.md:23-34);
+QuantizedAllToShardedLinear / QuantizedShardedToAllLinear are the quantized
+counterparts: column-parallel slices rows of (wq, scales, biases) per segment,
+row-parallel slices K at whole groups, nothing is re-quantized.
+
+One process per GPU.  The group is bootstrapped with torch.distributed (the
+env:// rendezvous: RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT, or the
+reference's MLX_RANK / MLX_WORLD_SIZE): every rank creates its P2P receive
+buffer (vmlx_tp_create), the CUDA IPC handles are exchanged with
+all_gather_object, and the data path (vmlx_tp_all_sum) never touches
+torch.distributed again.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import List, Optional
+
+import torch
+
+from . import _lib
+from ._lib import VMLXError, check
+from .llama import QuantLinear, shard_k, shard_rows
+from .ops import _stream
+
+IPC_HANDLE_BYTES = 64
+
+
+def _env_rank_world():
+    rank = int(os.environ.get("RANK", os.environ.get("MLX_RANK", "0")))
+    world = int(os.environ.get("WORLD_SIZE", os.environ.get("MLX_WORLD_SIZE", "1")))
+    return rank, world
+
+
+class Group:
+    """A tensor-parallel group of `size` ranks, one GPU each.
+
+    strict=False falls back to a size-1 group when no distributed environment
+    is set (Group.swift:21-24); strict=True raises instead."""
+
+    def __init__(self, strict: bool = False, backend: str = "nvlink", max_bytes: int = 4 << 20,
+                 exchange=None):
+        rank, world = _env_rank_world()
+        if world > 1 and exchange is None and not torch.distributed.is_initialized():
+            if strict and "MASTER_ADDR" not in os.environ:
+                raise VMLXError(_lib.VMLX_E_STATE, "distributed environment not set")
+            torch.distributed.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+        if world == 1 and strict and os.environ.get("WORLD_SIZE") is None and os.environ.get("MLX_WORLD_SIZE") is None:
+            raise VMLXError(_lib.VMLX_E_STATE, "strict group requested but no distributed environment")
+        self.rank, self.size, self.backend = rank, world, backend
+        self.max_bytes = max_bytes
+        self._exchange = exchange or self._torch_exchange
+        self._h = None
+        if world > 1:
+            self._connect()
+
+    @staticmethod
+    def _torch_exchange(blob: bytes) -> List[bytes]:
+        out = [None] * torch.distributed.get_world_size()
+        torch.distributed.all_gather_object(out, blob)
+        return out
+
+    def _connect(self):
+        h = ctypes.c_void_p()
+        check(_lib.lib().vmlx_tp_create(self.rank, self.size, self.max_bytes, ctypes.byref(h)))
+        self._h = h
+        buf = (ctypes.c_char * IPC_HANDLE_BYTES)()
+        check(_lib.lib().vmlx_tp_ipc_handle(h, buf))
+        handles = self._exchange(bytes(buf))
+        if len(handles) != self.size:
+            raise VMLXError(_lib.VMLX_E_STATE, "handle exchange returned the wrong count")
+        allh = (ctypes.c_char * (IPC_HANDLE_BYTES * self.size)).from_buffer_copy(b"".join(handles))
+        check(_lib.lib().vmlx_tp_open_peers(h, allh))
+
+    @property
+    def is_multi_rank(self) -> bool:
+        return self.size > 1
+
+    def all_sum(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Sum of x over the group's ranks (in place when out is x).  Identity for size 1."""
+        if self.size == 1:
+            return x if out is None else out.copy_(x)
+        out = x if out is None else out
+        check(_lib.lib().vmlx_tp_all_sum(self._h, out.data_ptr(), x.data_ptr(), x.numel(), _stream(x)))
+        return out
+
+    def status(self) -> int:
+        """VMLX_OK, or VMLX_E_PEER_TIMEOUT if a peer wait ran out since the last call (synchronous)."""
+        if self._h is None:
+            return _lib.VMLX_OK
+        code = ctypes.c_int(0)
+        check(_lib.lib().vmlx_tp_status(self._h, ctypes.byref(code)))
+        return code.value
+
+    def close(self):
+        if self._h is not None:
+            _lib.lib().vmlx_tp_destroy(self._h)
+            self._h = None
+
+
+class QuantizedAllToShardedLinear:
+    """Column-parallel quantized linear: rank r keeps output rows
+    [r*N/P, (r+1)*N/P) of every segment (LinearLayers.swift:59-105).  No collective."""
+
+    def __init__(self, ql: QuantLinear, group: Group, segments: Optional[List[int]] = None):
+        segs = segments or [ql.wq.shape[0]]
+        r, p = group.rank, group.size
+        self.local = QuantLinear(shard_rows(ql.wq, r, p, segs), shard_rows(ql.scales, r, p, segs),
+                                 shard_rows(ql.biases, r, p, segs), ql.group_size, ql.bits)
+        self.group = group
+
+    def __call__(self, x, out=None):
+        return self.local(x, out=out)
+
+
+class QuantizedShardedToAllLinear:
+    """Row-parallel quantized linear: rank r keeps input columns [r*K/P, (r+1)*K/P)
+    at whole groups (LinearLayers.swift:161-190); forward = partial matmul, allSum,
+    + bias once (:198-205)."""
+
+    def __init__(self, ql: QuantLinear, group: Group, bias: Optional[torch.Tensor] = None):
+        p = group.size
+        k = ql.wq.shape[-1] * 32 // ql.bits
+        if (k // p) % ql.group_size or k % p:
+            raise VMLXError(_lib.VMLX_E_INVALID, f"K={k} does not split into whole groups over {p} ranks")
+        r = group.rank
+        self.local = QuantLinear(shard_k(ql.wq, r, p), shard_k(ql.scales, r, p), shard_k(ql.biases, r, p),
+                                 ql.group_size, ql.bits)
+        self.group, self.bias = group, bias
+
+    def __call__(self, x_local, out=None):
+        y = self.local(x_local, out=out)
+        self.group.all_sum(y)
+        return y + self.bias if self.bias is not None else y
