@@ -107,6 +107,20 @@ VMLX_API int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t* 
                                const char* mode, int64_t M, int64_t N, int64_t K, void* stream);
 
 /*
+ * Decoder-block fusion of vmlx_cuda_quantized_matmul for decode (M <= 32):
+ *   x' = norm_weight * bf16(x * rsqrt(mean(x^2) + eps))   if norm_weight != NULL
+ *        (MLXFast.rmsNorm on the input, Llama.swift:118-127 `attention(norm(x))`)
+ *   y  = bf16(residual + bf16(x' @ dequantize(w)^T))     if residual != NULL
+ *        (the block's residual add; residual may alias y for an in-place update)
+ * Same rounding points as the separate kernels.  No counterpart as one call in
+ * the reference (MLX runs these as separate ops).
+ */
+VMLX_API int vmlx_cuda_quantized_matmul_fused(void* y, const void* x, const uint32_t* w, const void* scales,
+                                              const void* biases, int group_size, int bits, int64_t M, int64_t N,
+                                              int64_t K, const void* norm_weight, float eps, const void* residual,
+                                              void* stream);
+
+/*
  * Gathered quantized matmul over a stack of E expert matrices.
  * Replaces mlx_gather_qmm (Source/Cmlx/include/mlx/c/ops.h:475-488), the op
  * behind QuantizedSwitchLinear.callAsFunction
@@ -182,7 +196,7 @@ VMLX_API int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache
  * code that must not risk a cudaMalloc mid-decode).  The per-split partials
  * live in an 8 MiB array inside the library's device image (held on every GPU
  * that loads the library until the process exits); calls needing more
- * (batch * n_heads * min(64, ceil(kv_len/256)) * (head_dim + 2) * 4 bytes) are
+ * (batch * n_heads * min(128, ceil(kv_len/128)) * (head_dim + 2) * 4 bytes) are
  * rejected with VMLX_E_INVALID.  The first call on a device looks up the
  * array's address with that device current, so make it before any stream
  * capture.  All calls on a device share the array: calls that may overlap on

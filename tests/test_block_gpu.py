@@ -111,10 +111,11 @@ def _layer_ref(orc, dec, x, pos):
     return x
 
 
-def test_decoder_step_matches_reference(vm, orc, cuda):
+@pytest.mark.parametrize("fused", [False, True])
+def test_decoder_step_matches_reference(vm, orc, cuda, fused):
     cfg = vm.llama.LlamaConfig(hidden=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1024, n_layers=2)
     B, pos = 3, 64
-    dec = vm.llama.LlamaDecoder(cfg, B, max_len=96, dev=cuda, seed=5, cache_fill=pos)
+    dec = vm.llama.LlamaDecoder(cfg, B, max_len=96, dev=cuda, seed=5, cache_fill=pos, fused=fused)
     g = torch.Generator(cuda).manual_seed(9)
     x = torch.randn(B, cfg.hidden, device=cuda, generator=g).bfloat16()
     x0 = f(x)
@@ -142,3 +143,23 @@ def test_decoder_step_cuda_graph_replay(vm, orc, cuda):
         gph.replay()
     torch.cuda.synchronize()
     assert torch.equal(xg, eager)
+
+
+@pytest.mark.parametrize("M", [1, 4, 9])
+def test_fused_gemv_matches_separate_kernels(vm, orc, cuda, M):
+    """RMSNorm-on-load and residual-on-store fusions equal the separate kernels
+    up to the last bit of 1/rms (tolerance) for 4-bit (CUDA-core and MMA paths) and 8-bit."""
+    K, N = 2048, 512
+    g = torch.Generator(cuda).manual_seed(M)
+    for bits in (4, 8):
+        w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+        wq, s, b = vm.quantized(w, bits=bits)
+        x = (torch.randn(M, K, device=cuda, generator=g) * 2).bfloat16()
+        nw = (1 + 0.1 * torch.randn(K, device=cuda, generator=g)).bfloat16()
+        res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+        ref = vm.fast.add(res, vm.quantized_mm(vm.fast.rms_norm(x, nw, 1e-5), wq, s, b, bits=bits))
+        got = vm.ops.quantized_mm_fused(x, wq, s, b, bits=bits, norm_weight=nw, eps=1e-5, residual=res)
+        check(f(got), f(ref))
+        y = res.clone()
+        vm.ops.quantized_mm_fused(x, wq, s, b, bits=bits, norm_weight=nw, residual=y, out=y)  # in place
+        assert torch.equal(y, got)

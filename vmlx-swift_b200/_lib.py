@@ -42,6 +42,8 @@ SIGNATURES = {
     "vmlx_cuda_dequantize": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, _i64, _int, _int, _str, _vp]),
     "vmlx_cuda_quantized_matmul": (
         _int, [_vp, _vp, _vp, _vp, _vp, _bool, _int, _int, _str, _i64, _i64, _i64, _vp]),
+    "vmlx_cuda_quantized_matmul_fused": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64, _vp, _c.c_float, _vp, _vp]),
     "vmlx_cuda_gather_qmm": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _bool, _int, _int, _str, _bool, _i64, _i64,
                _i64, _i64, _i64, _i64, _vp]),

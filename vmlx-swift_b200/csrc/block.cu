@@ -117,12 +117,15 @@ __global__ void rope_qkv_kernel(const bf16* __restrict__ qkv, bf16* __restrict__
 constexpr int SDPA_D = 128;
 constexpr int SDPA_SUB = 32;  // positions per shared-memory stage
 
+constexpr int SDPA_STAGES = 4;  // ring depth: 4 x (K + V) x 32 positions = 64 KB
+constexpr size_t SDPA_SMEM = (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16) + 64;
+
 __global__ void __launch_bounds__(256)
 sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
                    float* __restrict__ part, int Hq, int Hkv, int kv_len, int max_len, int chunk, float scale_log2) {
-  __shared__ __align__(128) bf16 ks[2][SDPA_SUB][SDPA_D];
-  __shared__ __align__(128) bf16 vs[2][SDPA_SUB][SDPA_D];
-  __shared__ uint64_t full[2];
+  extern __shared__ __align__(128) uint8_t sdpa_smem[];
+  bf16* ring = reinterpret_cast<bf16*>(sdpa_smem);  // [stage][K|V][SUB][D]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sdpa_smem + (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16));
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = Hq / Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,11 +138,26 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
   const bf16* vbase = vc + ((int64_t)b * Hkv + kvh) * max_len * SDPA_D;
 
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int s = 0; s < SDPA_STAGES; s++) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  // the cache and q may come from the previous kernel (launch overlap): wait for it
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  const int nsub = t1 > t0 ? (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB : 0;
+  auto kst = [&](int s) { return ring + ((size_t)(s % SDPA_STAGES) * 2 + 0) * SDPA_SUB * SDPA_D; };
+  auto vst = [&](int s) { return ring + ((size_t)(s % SDPA_STAGES) * 2 + 1) * SDPA_SUB * SDPA_D; };
+  auto issue = [&](int s) {
+    const int a = t0 + s * SDPA_SUB;
+    const int n = min(SDPA_SUB, t1 - a);
+    const uint32_t bytes = (uint32_t)n * SDPA_D * 2;
+    mbar_arrive_expect_tx(&full[s % SDPA_STAGES], 2 * bytes);
+    bulk_g2s(kst(s), kbase + (int64_t)a * SDPA_D, bytes, &full[s % SDPA_STAGES]);
+    bulk_g2s(vst(s), vbase + (int64_t)a * SDPA_D, bytes, &full[s % SDPA_STAGES]);
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < nsub && s < SDPA_STAGES; s++) issue(s);
 
   float qf[32];
   if (warp < G) {
@@ -160,27 +178,18 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
 #pragma unroll
   for (int i = 0; i < 32; i++) o[i] = 0.f;
 
-  const int nsub = (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB;
-  auto issue = [&](int s) {
-    const int a = t0 + s * SDPA_SUB;
-    const int n = min(SDPA_SUB, t1 - a);
-    const uint32_t bytes = (uint32_t)n * SDPA_D * 2;
-    mbar_arrive_expect_tx(&full[s & 1], 2 * bytes);
-    bulk_g2s(&ks[s & 1][0][0], kbase + (int64_t)a * SDPA_D, bytes, &full[s & 1]);
-    bulk_g2s(&vs[s & 1][0][0], vbase + (int64_t)a * SDPA_D, bytes, &full[s & 1]);
-  };
-  if (threadIdx.x == 0 && nsub > 0) issue(0);
   bool ok = true;
   for (int s = 0; s < nsub; s++) {
-    if (threadIdx.x == 0 && s + 1 < nsub) issue(s + 1);  // the other buffer was released at the end of s-1
-    ok &= mbar_wait(&full[s & 1], (s >> 1) & 1);
+    ok &= mbar_wait(&full[s % SDPA_STAGES], (s / SDPA_STAGES) & 1);
     const int n = min(SDPA_SUB, t1 - (t0 + s * SDPA_SUB));
     if (warp < G) {
+      const bf16* ks = kst(s);
+      const bf16* vs = vst(s);
       for (int pp = p; pp < SDPA_SUB; pp += 8) {
         const bool valid = pp < n;
         float d = 0.f;
         if (valid) {
-          const bf16* kr = &ks[s & 1][pp][pt * 32];
+          const bf16* kr = ks + pp * SDPA_D + pt * 32;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 v = *reinterpret_cast<const uint4*>(kr + i);
@@ -200,7 +209,7 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
           const float corr = exp2f(m - mn);
           const float pw = exp2f(d - mn);
           l = l * corr + pw;
-          const bf16* vr = &vs[s & 1][pp][pt * 32];
+          const bf16* vr = vs + pp * SDPA_D + pt * 32;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 v = *reinterpret_cast<const uint4*>(vr + i);
@@ -216,7 +225,8 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
         }
       }
     }
-    __syncthreads();  // buffer s&1 may be refilled by the issue of s+2
+    __syncthreads();  // stage s is free: refill it with sub s + STAGES
+    if (threadIdx.x == 0 && s + SDPA_STAGES < nsub) issue(s + SDPA_STAGES);
   }
   if (warp < G) {
     // merge the 8 position lanes that share `pt`
@@ -325,8 +335,38 @@ extern "C" int vmlx_cuda_rope_qkv(void* q_out, void* k_cache, void* v_cache, con
 }
 
 static int sdpa_splits(int64_t kv_len) {
-  int64_t s = (kv_len + 255) / 256;  // ~256 cache positions per CTA
-  return (int)(s < 1 ? 1 : (s > 64 ? 64 : s));
+  int64_t s = (kv_len + 127) / 128;  // ~128 cache positions per CTA
+  return (int)(s < 1 ? 1 : (s > 128 ? 128 : s));
+}
+
+static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, float* part, bf16* out, int64_t batch,
+                       int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    int rc = check_cuda(cudaFuncSetAttribute(sdpa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)SDPA_SMEM), "sdpa_decode: cudaFuncSetAttribute");
+    if (rc) return rc;
+    attr = true;
+  }
+  const int splits = sdpa_splits(kv_len);
+  const int chunk = (int)((kv_len + splits - 1) / splits);
+  const int G = n_heads / n_kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
+  cfg.blockDim = dim3(32 * G);
+  cfg.dynamicSmemBytes = SDPA_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  int rc = check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel, q, kc, vc, part, n_heads, n_kv_heads, (int)kv_len,
+                                         (int)max_len, chunk, scale * 1.4426950408889634f),
+                      "sdpa_decode_kernel launch");
+  if (rc) return rc;
+  sdpa_combine_kernel<<<(unsigned)(batch * n_heads), SDPA_D, 0, st>>>(part, out, splits);
+  return check_launch("sdpa_combine_kernel");
 }
 
 extern "C" size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int64_t kv_len, int head_dim) {
@@ -349,18 +389,8 @@ extern "C" int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cac
   if (workspace_bytes < need)
     return set_error(VMLX_E_INVALID, "sdpa_decode: workspace of %zu bytes, %zu needed", workspace_bytes, need);
   if (batch == 0) return VMLX_OK;
-  const int splits = sdpa_splits(kv_len);
-  const int chunk = (int)((kv_len + splits - 1) / splits);
-  const int G = n_heads / n_kv_heads;
-  cudaStream_t st = as_stream(stream);
-  dim3 grid((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
-  sdpa_decode_kernel<<<grid, 32 * G, 0, st>>>((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache,
-                                             (float*)workspace, n_heads, n_kv_heads, (int)kv_len, (int)max_len,
-                                             chunk, scale * 1.4426950408889634f);
-  int rc = check_launch("sdpa_decode_kernel");
-  if (rc) return rc;
-  sdpa_combine_kernel<<<(unsigned)(batch * n_heads), SDPA_D, 0, st>>>((const float*)workspace, (bf16*)out, splits);
-  return check_launch("sdpa_combine_kernel");
+  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, (float*)workspace, (bf16*)out,
+                     batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
 }
 
 extern "C" int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, int64_t ffn, void* stream) {
@@ -394,7 +424,7 @@ extern "C" int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n,
 // Limits and behaviour:
 //  * the array holds SDPA_NOALLOC_BYTES (8 MiB) per GPU, for as long as the
 //    process has the library loaded on that GPU; calls whose partials need
-//    more (batch * n_heads * ceil(kv_len/256, at most 64) * (head_dim + 2) * 4
+//    more (batch * n_heads * ceil(kv_len/128, at most 128) * (head_dim + 2) * 4
 //    bytes) are rejected with VMLX_E_INVALID;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
@@ -450,16 +480,6 @@ extern "C" int vmlx_cuda_sdpa_decode_noalloc(void* out, const void* q, const voi
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  const int splits = sdpa_splits(kv_len);
-  const int chunk = (int)((kv_len + splits - 1) / splits);
-  const int G = n_heads / n_kv_heads;
-  cudaStream_t st = as_stream(stream);
-  dim3 grid((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
-  sdpa_decode_kernel<<<grid, 32 * G, 0, st>>>((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache,
-                                             (float*)scratch, n_heads, n_kv_heads, (int)kv_len, (int)max_len, chunk,
-                                             scale * 1.4426950408889634f);
-  rc = check_launch("sdpa_decode_kernel (noalloc)");
-  if (rc) return rc;
-  sdpa_combine_kernel<<<(unsigned)(batch * n_heads), SDPA_D, 0, st>>>((const float*)scratch, (bf16*)out, splits);
-  return check_launch("sdpa_combine_kernel (noalloc)");
+  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, (float*)scratch, (bf16*)out,
+                     batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
 }

@@ -24,6 +24,10 @@ struct QmvArgs {
   int64_t x_batches;  // gather: number of x matrices
   int64_t n_experts;
   int* status;  // optional device word set to VMLX_E_STATE if a bounded wait ran out
+  // optional fusions (decoder block): RMSNorm of x on load, residual add on store
+  const bf16* norm_w;   // x <- norm_w * bf16(x * rsqrt(mean(x^2) + eps)) over the full row
+  float eps;
+  const bf16* residual;  // y <- bf16(residual + bf16(x @ W^T)), residual laid out like y (may alias y)
 };
 
 int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int toka, cudaStream_t st);

@@ -72,3 +72,18 @@ extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, c
   }
   return launch_qmv(a, QMV_GATHER, bits, group_size, batch, toka_for(M), st);
 }
+
+extern "C" int vmlx_cuda_quantized_matmul_fused(void* y, const void* x, const uint32_t* w, const void* scales,
+                                                const void* biases, int group_size, int bits, int64_t M, int64_t N,
+                                                int64_t K, const void* norm_weight, float eps, const void* residual,
+                                                void* stream) {
+  if (M == 0 && N > 0 && K > 0) return VMLX_OK;
+  int rc = check_mm_args(y, x, w, scales, biases, true, group_size, bits, "affine", M, N, K);
+  if (rc) return rc;
+  if (M > 32) return set_error(VMLX_E_UNSUPPORTED, "quantized_matmul_fused: M=%lld > 32", (long long)M);
+  if (norm_weight && (!aligned(norm_weight, 16) || K % 8))
+    return set_error(VMLX_E_INVALID, "quantized_matmul_fused: norm_weight must be 16-byte aligned, K a multiple of 8");
+  QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
+            M, N, K, 0, 1, 1, nullptr, (const bf16*)norm_weight, eps, (const bf16*)residual};
+  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, toka_for(M), as_stream(stream));
+}

@@ -129,6 +129,46 @@ __device__ __forceinline__ void ffma2(unsigned long long& acc, unsigned long lon
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
 }
 
+// RMSNorm applied to 8 consecutive bf16 of x at column k0 (same rounding as
+// rms_norm_kernel: n = bf16(x * inv), out = bf16(w * n)).
+__device__ __forceinline__ uint4 norm8(uint4 v, float inv, const bf16* w) {
+  const uint4 ww = *reinterpret_cast<const uint4*>(w);
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w}, wu[4] = {ww.x, ww.y, ww.z, ww.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
+    const float2 n = __bfloat1622float2(__floats2bfloat162_rn(f.x * inv, f.y * inv));
+    const float2 wf = __bfloat1622float2(u32_as_bf162(wu[j]));
+    o[j] = bf162_as_u32(__floats2bfloat162_rn(wf.x * n.x, wf.y * n.y));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+__device__ __forceinline__ uint2 norm4(uint2 v, float inv, const bf16* w) {
+  const uint2 ww = *reinterpret_cast<const uint2*>(w);
+  const uint32_t u[2] = {v.x, v.y}, wu[2] = {ww.x, ww.y};
+  uint32_t o[2];
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
+    const float2 n = __bfloat1622float2(__floats2bfloat162_rn(f.x * inv, f.y * inv));
+    const float2 wf = __bfloat1622float2(u32_as_bf162(wu[j]));
+    o[j] = bf162_as_u32(__floats2bfloat162_rn(wf.x * n.x, wf.y * n.y));
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+// Store one output element, with the optional fused residual add.
+__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v) {
+  if (p.residual) {
+    const bf16* rr = p.residual + (yr - p.y);
+    const float s = __bfloat162float(__float2bfloat16_rn(v));
+    yr[col] = __float2bfloat16_rn(__bfloat162float(rr[col]) + s);
+  } else {
+    yr[col] = __float2bfloat16_rn(v);
+  }
+}
+
 // Shared-memory plan of one CTA; sizes depend on the K-slice (ks groups) and
 // on the number of token rows staged at once (tok).  The ring is 1024-byte
 // aligned (the 128-byte TMA swizzle atom).
@@ -224,6 +264,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   uint64_t* scempty = scfull + 2;
   uint8_t* xfrag = smem + L.o_xfrag;
   float* xfrag_f = reinterpret_cast<float*>(xfrag);
+  __shared__ float xinv[32];  // fused RMSNorm: 1 / rms per staged token
   float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);
   const int TOKX = L.tokx;
   float* red = reinterpret_cast<float*>(smem + L.o_red);
@@ -338,6 +379,28 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         if (mode != QMV_DENSE || !x_staged || I.ntok > TOKA) {
           // stage x of this chunk in fragment order, with per-group sums
           named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous chunk
+          if (p.norm_w) {
+            // fused RMSNorm: 1 / rms of each token's full row (warp w takes tokens w, w+4, ...)
+            for (int tok = warp; tok < ntok; tok += QMV_CWARPS) {
+              const bf16* xr;
+              bf16* yr_unused;
+              token_rows(p, mode, I.base, chunk + tok, xr, yr_unused);
+              float ss = 0.f;
+              for (int64_t k = lane * 8; k < p.K; k += 256) {
+                const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                  const float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
+                  ss = fmaf(f.x, f.x, ss);
+                  ss = fmaf(f.y, f.y, ss);
+                }
+              }
+              for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+              if (lane == 0) xinv[tok] = rsqrtf(ss / (float)p.K + p.eps);
+            }
+            named_bar_sync(1, 32 * QMV_CWARPS);
+          }
           if constexpr (CC) {
             // fp32 x, 32 values per 16-byte weight chunk, plus the chunk's sum
             const int nch = nG * CPG;
@@ -355,6 +418,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
               for (int q = 0; q < 4; q++) {
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if (xrow) v = *reinterpret_cast<const uint4*>(xrow + q * 8);
+                if (xrow && p.norm_w) v = norm8(v, xinv[tok], p.norm_w + gs0 * GS + ci * 32 + q * 8);
                 const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
                 const float2 c2 = __bfloat1622float2(u32_as_bf162(v.z)), d2 = __bfloat1622float2(u32_as_bf162(v.w));
                 reinterpret_cast<float4*>(dst + q * 8)[0] = make_float4(a.x, a.y, b2.x, b2.y);
@@ -382,6 +446,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 if constexpr (BITS == 4) {
                   uint4 v = make_uint4(0, 0, 0, 0);
                   if (xrow) v = *reinterpret_cast<const uint4*>(xrow + cc * VPL + wi * 8);
+                  if (xrow && p.norm_w) v = norm8(v, xinv[tok], p.norm_w + (gs0 + gl) * GS + cc * VPL + wi * 8);
                   uint4 f;
                   f.x = prmt(v.x, v.y, 0x5410);  // (x0, x2)
                   f.y = prmt(v.z, v.w, 0x5410);  // (x4, x6)
@@ -394,6 +459,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 } else {
                   uint2 v = make_uint2(0, 0);
                   if (xrow) v = *reinterpret_cast<const uint2*>(xrow + cc * VPL + wi * 4);
+                  if (xrow && p.norm_w) v = norm4(v, xinv[tok], p.norm_w + (gs0 + gl) * GS + cc * VPL + wi * 4);
                   *reinterpret_cast<uint2*>(dst) = v;
                   const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
                   sum += (a.x + a.y) + (b2.x + b2.y);
@@ -509,7 +575,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 const bf16* xr_unused;
                 bf16* yr;
                 token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-                yr[row] = __float2bfloat16_rn(acc[t][j]);
+                store_y(p, yr, row, acc[t][j]);
               }
             }
           }
@@ -618,7 +684,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                     const bf16* xr_unused;
                     bf16* yr;
                     token_rows(p, mode, I.base, chunk + t, xr_unused, yr);
-                    yr[I.n0 + r] = __float2bfloat16_rn(res[j][t]);
+                    store_y(p, yr, I.n0 + r, res[j][t]);
                   }
                 } else {
                   rb[r * TOKA + t] = res[j][t];
@@ -639,7 +705,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
               const bf16* xr_unused;
               bf16* yr;
               token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-              yr[I.n0 + r] = __float2bfloat16_rn(s);
+              store_y(p, yr, I.n0 + r, s);
             }
           }
           red_count++;

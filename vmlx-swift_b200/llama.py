@@ -53,6 +53,11 @@ class QuantLinear:
         return ops.quantized_mm(x, self.wq, self.scales, self.biases, group_size=self.group_size,
                                 bits=self.bits, out=out)
 
+    def fused(self, x, norm_weight=None, eps=1e-5, residual=None, out=None):
+        """x -> [RMSNorm] -> matmul -> [+ residual], one kernel (decode, M <= 32)."""
+        return ops.quantized_mm_fused(x, self.wq, self.scales, self.biases, group_size=self.group_size,
+                                      bits=self.bits, norm_weight=norm_weight, eps=eps, residual=residual, out=out)
+
 
 def shard_rows(t: torch.Tensor, rank: int, world: int, segments: List[int]) -> torch.Tensor:
     """Column-parallel slice (AllToShardedLinear, LinearLayers.swift:59-105): each
@@ -113,11 +118,14 @@ class LlamaDecoder:
     """Decoder stack with per-layer bf16 KV caches [B, Hkv/P, max_len, D]."""
 
     def __init__(self, cfg: LlamaConfig, batch: int, max_len: int, dev, seed: int = 0,
-                 rank: int = 0, world: int = 1, all_sum=None, cache_fill: int = 0):
+                 rank: int = 0, world: int = 1, all_sum=None, cache_fill: int = 0, fused: bool = True):
         if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn % world:
             raise ValueError("heads / ffn not divisible by the TP size")
         self.cfg, self.B, self.max_len, self.dev = cfg, batch, max_len, dev
         self.rank, self.world, self.all_sum = rank, world, all_sum
+        # fused: RMSNorm folded into the q/k/v and gate/up GEMVs (x staged normalised), and at TP=1
+        # the residual adds folded into the o_proj / down_proj GEMVs (in place on x)
+        self.fused = fused and batch <= 32
         self.hq, self.hkv, self.ffn = cfg.n_heads // world, cfg.n_kv_heads // world, cfg.ffn // world
         gen = torch.Generator(device=dev).manual_seed(seed)
         self.layers = [LlamaLayerWeights(cfg, dev, gen, rank, world) for _ in range(cfg.n_layers)]
@@ -156,29 +164,47 @@ class LlamaDecoder:
     def step(self, x: torch.Tensor, pos: int) -> torch.Tensor:
         """One decode step for B tokens at cache position `pos` (in place on x)."""
         cfg = self.cfg
+        fused, tp = self.fused, self.world > 1
         for i, L in enumerate(self.layers):
-            fast.rms_norm(x, L.norm1, cfg.eps, out=self.h)
-            L.qkv(self.h, out=self.qkv_buf)
+            if fused:
+                L.qkv.fused(x, norm_weight=L.norm1, eps=cfg.eps, out=self.qkv_buf)
+            else:
+                fast.rms_norm(x, L.norm1, cfg.eps, out=self.h)
+                L.qkv(self.h, out=self.qkv_buf)
             fast.rope_qkv(self.qkv_buf, self.k_cache[i], self.v_cache[i], self.hq, self.hkv, pos,
                           base=cfg.rope_theta, q_out=self.q)
             fast.sdpa_decode(self.q, self.k_cache[i], self.v_cache[i], pos + 1, workspace=self.ws,
                              out=self.attn)
-            L.o(self.attn.view(self.B, -1), out=self.proj)
-            self._reduce(self.proj)
-            fast.add(x, self.proj, out=x)
-            fast.rms_norm(x, L.norm2, cfg.eps, out=self.h)
-            L.gate_up(self.h, out=self.gu)
+            if fused and not tp:
+                L.o.fused(self.attn.view(self.B, -1), residual=x, out=x)
+            else:
+                L.o(self.attn.view(self.B, -1), out=self.proj)
+                self._reduce(self.proj)
+                fast.add(x, self.proj, out=x)
+            if fused:
+                L.gate_up.fused(x, norm_weight=L.norm2, eps=cfg.eps, out=self.gu)
+            else:
+                fast.rms_norm(x, L.norm2, cfg.eps, out=self.h)
+                L.gate_up(self.h, out=self.gu)
             fast.silu_mul(self.gu, out=self.act)
-            L.down(self.act, out=self.proj)
-            self._reduce(self.proj)
-            fast.add(x, self.proj, out=x)
+            if fused and not tp:
+                L.down.fused(self.act, residual=x, out=x)
+            else:
+                L.down(self.act, out=self.proj)
+                self._reduce(self.proj)
+                fast.add(x, self.proj, out=x)
         return x
 
     # ---- CUDA-graph decode (the public per-token call) ----
     @property
     def launches_per_step(self):
-        # per layer: 2 rms_norm, 4 GEMV, rope, sdpa (2 kernels), silu_mul, 2 add (+ 2 all-reduce under TP)
-        return self.cfg.n_layers * (12 + (2 if self.world > 1 else 0))
+        # per layer: 4 GEMV, rope, sdpa (2 kernels), silu_mul; unfused: + 2 rms_norm; TP: + 2 all-reduce + 2 add
+        n = 8 + (0 if self.fused else 2)
+        if self.world > 1:
+            n += 4
+        elif not self.fused:
+            n += 2
+        return self.cfg.n_layers * n
 
     def capture(self, x: torch.Tensor, pos: int, stream=None) -> "torch.cuda.CUDAGraph":
         """Capture step(x, pos) on `stream` into a CUDA graph (x is the graph's

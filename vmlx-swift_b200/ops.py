@@ -117,6 +117,26 @@ def quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases:
     return out
 
 
+def quantized_mm_fused(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                       group_size: int = 64, bits: int = 4, norm_weight: Optional[torch.Tensor] = None,
+                       eps: float = 1e-5, residual: Optional[torch.Tensor] = None,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode-block fusion: optional RMSNorm of x on load and residual add on store
+    (M <= 32).  ``out`` may be ``residual`` for an in-place ``x += W @ norm(h)``."""
+    _need_cuda(x, w, scales, biases, norm_weight, residual)
+    x = x.contiguous()
+    K = x.shape[-1]
+    N = w.shape[-2]
+    M = x.numel() // K if K else 0
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    check(_lib.lib().vmlx_cuda_quantized_matmul_fused(
+        out.data_ptr(), x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), group_size, bits,
+        M, N, K, norm_weight.data_ptr() if norm_weight is not None else None, eps,
+        residual.data_ptr() if residual is not None else None, _stream(x)))
+    return out
+
+
 def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                         biases: Optional[torch.Tensor], lhs_indices: Optional[torch.Tensor] = None,
                         rhs_indices: Optional[torch.Tensor] = None, transpose: bool = True,
