@@ -742,7 +742,7 @@ static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   L.init(BITS, GS, ks, toka, CC);
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);  // + static smem <= 227 KB
     if (e != cudaSuccess) return check_cuda(e, "qmv: cudaFuncSetAttribute");
     attr_set = true;
   }
@@ -820,7 +820,7 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     const int ks = slice_groups(KG, C, SG);
     if ((KG + ks - 1) / ks != C) continue;  // this C rounds to another one
     const size_t sm = smem_of(ks, toka);
-    if (sm > 227 * 1024) continue;
+    if (sm > 226 * 1024) continue;
     int per_sm = (int)((228 * 1024) / (sm + 1024));
     const int reg_cap = cc ? 2 : 3;  // 160 threads x ~150 (CUDA-core) / ~128 (MMA) registers
     per_sm = per_sm > reg_cap ? reg_cap : (per_sm < 1 ? 1 : per_sm);
@@ -834,8 +834,8 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
   int C = bestC;
 
   int ks = slice_groups(KG, C, SG);
-  while (smem_of(ks, toka) > 227 * 1024 && toka > 8) toka -= 8;
-  if (smem_of(ks, toka) > 227 * 1024)
+  while (smem_of(ks, toka) > 226 * 1024 && toka > 8) toka -= 8;
+  if (smem_of(ks, toka) > 226 * 1024)
     return set_error(VMLX_E_UNSUPPORTED, "qmv: K=%lld too large for the shared-memory plan", (long long)a.K);
   C = (int)((KG + ks - 1) / ks);
   if constexpr (BITS == 4) {
