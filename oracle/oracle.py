@@ -131,6 +131,17 @@ def qmm_f64(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
     return y
 
 
+def qmm_bf16w_f64(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """The tiled qmm's semantics (M > 32): W dequantized to the activation dtype
+    first -- QuantizedBlockLoader writes dequantize<T>() results, T = bfloat16,
+    to threadgroup memory (Source/Cmlx/mlx-generated/metal/quantized.h:525-560,
+    :670-720) -- then a matmul with wide accumulation (fp64 here).  Each weight
+    is rounded once to bf16 from the exact s*q + b."""
+    w = round_bf16(dequantize(wq, scales, biases, group_size, bits)).astype(np.float64)
+    x = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16)).astype(np.float64)
+    return x @ w.T
+
+
 def qmm_fp32_bf16(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
     """MLX-factorised fp32 GEMV (OpenMP), bf16 bit-pattern output [M, N]."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)

@@ -134,8 +134,50 @@ def test_quantized_mm_llama_ffn_shapes(vm, orc, cuda, M):
         xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
         y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=64, bits=4)
         rows = np.arange(0, N, 37)  # the fp64 oracle on a sample of output columns
-        ref = orc.qmm_f64(xb, u32(wq)[rows], bits_of(s)[rows], bits_of(b)[rows], 64, 4)
+        qmm = orc.qmm_f64 if M <= 32 else orc.qmm_bf16w_f64  # GEMV vs tiled-GEMM semantics
+        ref = qmm(xb, u32(wq)[rows], bits_of(s)[rows], bits_of(b)[rows], 64, 4)
         check_close(y.float().cpu().numpy()[:, rows], ref)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M", [33, 128, 300])
+def test_quantized_mm_tensor_core(vm, orc, cuda, bits, gs, M):
+    """M > 32 runs the tcgen05 GEMM (bf16 dequantized W tiles, fp32 TMEM
+    accumulation): ragged M and N tiles, several K stages."""
+    N, K = 272, 1024 + 2 * gs
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, gs, bits, 61 + M)
+    rng = np.random.default_rng(7 + M)
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
+    y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=gs, bits=bits)
+    ref = orc.qmm_bf16w_f64(xb, u32(wq), bits_of(s), bits_of(b), gs, bits)
+    check_close(y.float().cpu().numpy(), ref)
+    # against exact (unrounded) weights the bf16 weight tiles cost a little more: the max bar still holds
+    exact = orc.qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), gs, bits)
+    assert np.abs(y.float().cpu().numpy() - exact).max() / np.abs(exact).max() <= MAX_REL
+
+
+def test_tensor_core_rows_independent(vm, orc, cuda):
+    """Tensor-core regime: results are deterministic and a token's output does not
+    depend on the tile or call it lands in for a fixed K split (4 here for all three
+    calls): one 300-row call equals 128 + 172-row calls."""
+    K, N = 2048, 640
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 71)
+    x = torch.randn(300, K, device=cuda, generator=torch.Generator(cuda).manual_seed(1)).bfloat16()
+    full = vm.quantized_mm(x, wq, s, b)
+    parts = torch.cat([vm.quantized_mm(x[:128], wq, s, b), vm.quantized_mm(x[128:], wq, s, b)])
+    assert torch.equal(full, parts)
+    assert torch.equal(full, vm.quantized_mm(x, wq, s, b))
+
+
+def test_tensor_core_fallback_shape(vm, orc, cuda):
+    """K not a multiple of the 64-wide stage falls back to the GEMV kernel in passes."""
+    M, N, K, gs = 40, 96, 1056, 32
+    wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, gs, 4, 81)
+    rng = np.random.default_rng(3)
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
+    y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=gs, bits=4)
+    check_close(y.float().cpu().numpy(), orc.qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), gs, 4))
 
 
 def test_batch_invariance(vm, orc, cuda):

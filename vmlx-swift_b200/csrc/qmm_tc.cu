@@ -1,10 +1,371 @@
-// qmm_tc.cu -- tensor-core (tcgen05) GEMM for M > 32 (placeholder dispatch).
+// qmm_tc.cu -- tcgen05 / TMEM tensor-core GEMM for prefill and batched tiles (M > 32).
+//
+// y[M, N] = x[M, K] @ dequantize(W[N, K])^T, the op of MLX's affine_qmm_t
+// (Source/Cmlx/mlx-generated/metal/quantized.h:1136-1261, 1756-1813): like the
+// reference, W tiles are dequantized to the activation dtype (bf16,
+// QuantizedBlockLoader / dequantize, :525-739) and multiplied on the matrix
+// units with fp32 accumulation.
+//
+// One CTA computes a 128 (weight rows) x BT (tokens) tile of y^T over one K
+// split; S > 1 splits of a tile form a thread-block cluster and reduce through
+// distributed shared memory in a fixed order (deterministic):
+//   warp 0    TMA producer: x tile [BT tokens x 64 k] (128-byte swizzle = the
+//             UMMA K-major SW128 layout) and the raw packed W tile [128 rows x
+//             64 k] into rings completing on mbarriers;
+//   warp 1    allocates BT TMEM columns; one thread issues tcgen05.mma
+//             (kind::f16, M=128, N=BT, K=16, A = dequantized W, B = x, both
+//             K-major from shared memory) and tcgen05.commit to free stages;
+//   warps 4-11 dequantize: warp group h (0, 1) owns k [32h, 32h+32) of every
+//             stage, thread t weight row t; codes become bf16 scale*q + bias
+//             written into the SW128 A tile.  After the K loop they move the
+//             fp32 accumulator TMEM -> shared memory (token-major);
+//   all warps reduce the S splits and store bf16 y with coalesced 8-byte stores.
+// No multicast anywhere (this path may run in multi-GPU processes).
+#include <cooperative_groups.h>
+
 #include "kernels.cuh"
+#include "sm100_util.cuh"
+#include "tmap.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace vmlx {
-int launch_qmm_tc(const bf16*, const uint32_t*, const bf16*, const bf16*, bf16*, int64_t, int64_t,
-                  int64_t, int, int, cudaStream_t, bool* handled) {
+
+int sm_count();
+
+constexpr int TC_BN = 128;  // weight rows per tile (UMMA M)
+constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row of bf16)
+constexpr int TC_SX = 3;    // x stages
+constexpr int TC_SR = 4;    // raw W stages
+constexpr int TC_SA = 2;    // dequantized A stages
+constexpr int TC_WARPS = 12;
+constexpr int TC_THREADS = TC_WARPS * 32;
+constexpr int TC_DQ = 256;  // dequantizing threads (warps 4-11)
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  // start address >> 4 | LBO (unused for swizzled K-major, 1) | SBO = 1024 B between
+  // 8-row groups | descriptor version 1 | layout SWIZZLE_128B
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128.
+__host__ __device__ constexpr uint32_t tc_idesc(int bt) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bt >> 3) << 17) | ((uint32_t)(TC_BN >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 8 4-bit codes (one packed word, LSB first) -> 8 bf16 s*q + b, each rounded once.
+// Codes are made exact as bf16 128+q (high byte 0x43, q in the low mantissa bits).
+__device__ __forceinline__ uint4 dq8_4bit(uint32_t w, bf162 s2, bf162 b2) {
+  const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;  // even / odd codes per byte
+  const bf162 c128 = u32_as_bf162(0x43004300u);
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const uint32_t sel = (uint32_t)j | ((uint32_t)j << 4) | ((uint32_t)(4 + j) << 8) | ((uint32_t)(4 + j) << 12);
+    const uint32_t pr = (prmt(lo, hi, sel) & 0x00FF00FFu) | 0x43004300u;  // (q_2j, q_2j+1) as 128+q
+    o[j] = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(pr), c128), s2, b2));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// 8 8-bit codes (two words) -> 8 bf16: code byte into an fp32 2^23 + q, exact q,
+// fp32 s*q + b (s*q exact), rounded to bf16 -- the oracle's order of operations.
+__device__ __forceinline__ uint4 dq8_8bit(uint32_t w0, uint32_t w1, float s, float b) {
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const uint32_t w = j < 2 ? w0 : w1;
+    const uint32_t i0 = (j & 1) * 2;
+    const float f0 = __uint_as_float(prmt(w, 0x4B000000u, 0x7440u | i0)) - 8388608.f;
+    const float f1 = __uint_as_float(prmt(w, 0x4B000000u, 0x7440u | (i0 + 1))) - 8388608.f;
+    o[j] = bf162_as_u32(__floats2bfloat162_rn(__fadd_rn(__fmul_rn(f0, s), b), __fadd_rn(__fmul_rn(f1, s), b)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int BITS, int BT>
+struct TcLayout {
+  static constexpr int RAWB = TC_BK * BITS / 8;  // packed bytes per weight row per stage
+  static constexpr int XS = BT * 128;            // x stage bytes
+  static constexpr int AS = TC_BN * 128;         // A stage bytes
+  static constexpr int RS = TC_BN * RAWB;        // raw stage bytes
+  static constexpr int RING = TC_SX * XS + TC_SA * AS + TC_SR * RS;
+  static constexpr int RED = BT * TC_BN * 4;     // fp32 accumulator, token-major
+  static constexpr int DATA = RING > RED ? RING : RED;
+  static constexpr int BARS = (2 * TC_SX + 2 * TC_SR + 2 * TC_SA + 1) * 8 + 16;
+  static constexpr size_t SMEM = (size_t)DATA + BARS + 1024;
+};
+
+template <int BITS, int GS, int BT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+              const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y,
+              int M, int N, int K, int S, int* status) {
+  using L = TcLayout<BITS, BT>;
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
+  uint8_t* xs = smem;
+  uint8_t* as = xs + TC_SX * L::XS;
+  uint8_t* raw = as + TC_SA * L::AS;
+  float* red = reinterpret_cast<float*>(smem);  // reuses the rings once the K loop is done
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::DATA);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + TC_SX;
+  uint64_t* r_full = x_empty + TC_SX;
+  uint64_t* r_empty = r_full + TC_SR;
+  uint64_t* a_full = r_empty + TC_SR;
+  uint64_t* a_empty = a_full + TC_SA;
+  uint64_t* acc_full = a_empty + TC_SA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = (int)blockIdx.x % S;
+  const int n0 = ((int)blockIdx.x / S) * TC_BN, m0 = (int)blockIdx.y * BT;
+  const int KB = K / TC_BK;
+  const int kb0 = (int)((int64_t)split * KB / S), nkb = (int)((int64_t)(split + 1) * KB / S) - kb0;
+  const int KG = K / GS;
+
+  if (tid == 0) {
+    for (int i = 0; i < TC_SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < TC_SR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], TC_DQ / 32); }
+    for (int i = 0; i < TC_SA; i++) { mbar_init(&a_full[i], TC_DQ / 32); mbar_init(&a_empty[i], 1); }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmx);
+    tma_prefetch_desc(&tmw);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // Setup above overlaps the previous kernel's tail under programmatic launch; from here on
+  // this grid reads x and writes y.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; i++) {
+        const int kb = kb0 + i, sx = i % TC_SX, sr = i % TC_SR;
+        if (i >= TC_SR) ok &= mbar_wait(&r_empty[sr], ((i / TC_SR) - 1) & 1);
+        mbar_arrive_expect_tx(&r_full[sr], L::RS);
+        tma_load_2d(raw + (size_t)sr * L::RS, &tmw, kb * L::RAWB, n0, &r_full[sr]);
+        if (i >= TC_SX) ok &= mbar_wait(&x_empty[sx], ((i / TC_SX) - 1) & 1);
+        mbar_arrive_expect_tx(&x_full[sx], L::XS);
+        tma_load_2d(xs + (size_t)sx * L::XS, &tmx, kb * TC_BK, m0, &x_full[sx]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc_idesc(BT);
+      for (int i = 0; i < nkb; i++) {
+        const int sx = i % TC_SX, sa = i % TC_SA;
+        ok &= mbar_wait(&a_full[sa], (i / TC_SA) & 1);
+        ok &= mbar_wait(&x_full[sx], (i / TC_SX) & 1);
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(as + (size_t)sa * L::AS);
+        const uint32_t b_addr = smem_u32(xs + (size_t)sx * L::XS);
+#pragma unroll
+        for (int k = 0; k < TC_BK / 16; k++)
+          umma_f16(tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                   (i | k) ? 1u : 0u);
+        umma_commit(&a_empty[sa]);
+        umma_commit(&x_empty[sx]);
+      }
+      umma_commit(acc_full);
+    }
+  } else if (warp >= 4) {
+    // ---------------- dequantize W into the SW128 A tile ----------------
+    const int dq = tid - 128;
+    const int h = dq >> 7;   // k half of the stage
+    const int r = dq & 127;  // weight row within the tile
+    const int row = n0 + r < N ? n0 + r : N - 1;
+    const bf16* srow = scales + (int64_t)row * KG;
+    const bf16* brow = biases + (int64_t)row * KG;
+    for (int i = 0; i < nkb; i++) {
+      const int kb = kb0 + i, sr = i % TC_SR, sa = i % TC_SA;
+      const int g = (kb * TC_BK + h * 32) / GS;  // 32 k never straddle a group (GS >= 32)
+      const bf16 sv = srow[g], bv = brow[g];
+      ok &= mbar_wait(&r_full[sr], (i / TC_SR) & 1);
+      const uint8_t* rp = raw + (size_t)sr * L::RS + r * L::RAWB + h * (L::RAWB / 2);
+      uint32_t wv[BITS];  // this half's 32 codes: 4 words (4-bit) or 8 words (8-bit)
+#pragma unroll
+      for (int v = 0; v < BITS / 4; v++) {
+        const uint4 u = *reinterpret_cast<const uint4*>(rp + v * 16);
+        wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&r_empty[sr]);
+      if (i >= TC_SA) ok &= mbar_wait(&a_empty[sa], ((i / TC_SA) - 1) & 1);
+      uint8_t* arow = as + (size_t)sa * L::AS + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const int chunk = h * 4 + c;  // 8 bf16 = 16 bytes; stored at (chunk ^ (r & 7)) (128-byte swizzle)
+        uint4 o;
+        if constexpr (BITS == 4) {
+          o = dq8_4bit(wv[c], __bfloat162bfloat162(sv), __bfloat162bfloat162(bv));
+        } else {
+          o = dq8_8bit(wv[2 * c], wv[2 * c + 1], __bfloat162float(sv), __bfloat162float(bv));
+        }
+        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = o;
+      }
+      fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[sa]);
+    }
+    // ---------------- accumulator: TMEM -> shared memory (token-major) ----------------
+    ok &= mbar_wait(acc_full, 0);
+    tc_fence_after();
+    const int q4 = warp & 3;  // TMEM lanes 32*q4 .. +31 = weight rows
+    const int rr = q4 * 32 + lane;
+    for (int c0 = h * (BT / 2); c0 < (h + 1) * (BT / 2); c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+      for (int j = 0; j < 16; j++) red[(c0 + j) * TC_BN + rr] = __uint_as_float(v[j]);
+    }
+  }
+  tc_fence_before();
+  if (S > 1) {
+    cluster_arrive();
+    cluster_wait();
+  } else {
+    __syncthreads();
+  }
+  // ---------------- reduce the splits (fixed order) and store bf16 y ----------------
+  {
+    const int t_lo = split * BT / S, t_hi = (split + 1) * BT / S;
+    const int n = n0 + 4 * lane;
+    const bool vec = (N & 3) == 0 && n + 4 <= N;
+    cg::cluster_group cluster = cg::this_cluster();
+    for (int t = t_lo + warp; t < t_hi; t += TC_WARPS) {
+      const int m = m0 + t;
+      if (m >= M) break;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < S; q++) {
+        const float* src = S > 1 ? cluster.map_shared_rank(red, q) : red;
+        const float4 v = *reinterpret_cast<const float4*>(src + t * TC_BN + 4 * lane);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      bf16* yr = y + (int64_t)m * N;
+      if (vec) {
+        const bf162 a = __floats2bfloat162_rn(acc.x, acc.y), b = __floats2bfloat162_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(yr + n) = make_uint2(bf162_as_u32(a), bf162_as_u32(b));
+      } else {
+        const float e[4] = {acc.x, acc.y, acc.z, acc.w};
+        for (int j = 0; j < 4; j++)
+          if (n + j < N) yr[n + j] = __float2bfloat16_rn(e[j]);
+      }
+    }
+  }
+  if (S > 1) {  // keep this CTA's shared memory alive until every split has read it
+    cluster_arrive();
+    cluster_wait();
+  }
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT));
+  if (!ok && status) atomicExch(status, VMLX_E_STATE);
+}
+
+template <int BITS, int GS, int BT>
+static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y, int64_t M,
+                     int64_t N, int64_t K, cudaStream_t st) {
+  using L = TcLayout<BITS, BT>;
+  auto kern = qmm_tc_kernel<BITS, GS, BT>;
+  static bool attr = false;
+  if (!attr) {
+    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM),
+                        "qmm_tc: cudaFuncSetAttribute");
+    if (rc) return rc;
+    attr = true;
+  }
+  CUtensorMap tmx, tmw;
+  if (!make_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TC_BK,
+                    BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K * BITS / 8, (uint64_t)N,
+                    (uint64_t)K * BITS / 8, L::RAWB, TC_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VMLX_E_CUDA;
+  // K splits: fill the SMs when the tile grid is small; each split keeps >= 8 stages.
+  const int64_t ntn = (N + TC_BN - 1) / TC_BN, ntm = (M + BT - 1) / BT;
+  const int64_t tiles = ntn * ntm, KB = K / TC_BK;
+  int S = 1;
+  while (S < 8 && tiles * S * 2 <= sm_count() && KB / (S * 2) >= 8) S *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(ntn * S), (unsigned)ntm, 1);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = L::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = (unsigned)S;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = launch_overlap() ? 2 : 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, tmx, tmw, scales, biases, y, (int)M, (int)N, (int)K, S,
+                                       (int*)nullptr),
+                    "qmm_tc_kernel launch");
+}
+
+template <int BITS, int GS>
+static int launch_bt(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int64_t M, int64_t N,
+                     int64_t K, cudaStream_t st) {
+  // 256-token tiles halve the dequantization per flop once M fills them and the grid stays wide
+  if (M > 128 && ((N + TC_BN - 1) / TC_BN) * ((M + 255) / 256) >= sm_count() / 2)
+    return launch_tc<BITS, GS, 256>(x, w, s, b, y, M, N, K, st);
+  if (M > 64) return launch_tc<BITS, GS, 128>(x, w, s, b, y, M, N, K, st);
+  return launch_tc<BITS, GS, 64>(x, w, s, b, y, M, N, K, st);
+}
+
+int launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y, int64_t M,
+                  int64_t N, int64_t K, int bits, int gs, cudaStream_t st, bool* handled) {
+  *handled = false;
+  if (K % TC_BK || !aligned(x, 16) || !aligned(w, 16) || (M + 63) / 64 > 65535 || M > (1ll << 30) ||
+      N > (1ll << 30) || K > (1ll << 30))
+    return VMLX_OK;  // shapes outside the tile plan run on the GEMV kernel in passes
+  *handled = true;
+  if (bits == 4 && gs == 32) return launch_bt<4, 32>(x, w, scales, biases, y, M, N, K, st);
+  if (bits == 4 && gs == 64) return launch_bt<4, 64>(x, w, scales, biases, y, M, N, K, st);
+  if (bits == 4 && gs == 128) return launch_bt<4, 128>(x, w, scales, biases, y, M, N, K, st);
+  if (bits == 8 && gs == 32) return launch_bt<8, 32>(x, w, scales, biases, y, M, N, K, st);
+  if (bits == 8 && gs == 64) return launch_bt<8, 64>(x, w, scales, biases, y, M, N, K, st);
+  if (bits == 8 && gs == 128) return launch_bt<8, 128>(x, w, scales, biases, y, M, N, K, st);
   *handled = false;
   return VMLX_OK;
 }
+
 }  // namespace vmlx
