@@ -6,19 +6,26 @@
 // QuantizedBlockLoader / dequantize, :525-739) and multiplied on the matrix
 // units with fp32 accumulation.
 //
-// One CTA computes a 128 (weight rows) x BT (tokens) tile of y^T over one K
+// One CTA computes a 256 (weight rows) x BT (tokens) tile of y^T over one K
 // split; S > 1 splits of a tile form a thread-block cluster and reduce through
-// distributed shared memory in a fixed order (deterministic):
+// distributed shared memory in a fixed order (deterministic).  Every weight
+// tile streams all of x from L2, so x traffic per flop falls as 1/rows-per-tile:
+// 256 rows (two M=128 MMAs sharing each x stage) keep it inside L2 bandwidth.
 //   warp 0    TMA producer: x tile [BT tokens x 64 k] (128-byte swizzle = the
-//             UMMA K-major SW128 layout) and the raw packed W tile [128 rows x
+//             UMMA K-major SW128 layout) and the raw packed W tile [256 rows x
 //             64 k] into rings completing on mbarriers;
-//   warp 1    allocates BT TMEM columns; one thread issues tcgen05.mma
-//             (kind::f16, M=128, N=BT, K=16, A = dequantized W, B = x, both
-//             K-major from shared memory) and tcgen05.commit to free stages;
-//   warps 4-11 dequantize: warp group h (0, 1) owns k [32h, 32h+32) of every
-//             stage, thread t weight row t; codes become bf16 scale*q + bias
-//             written into the SW128 A tile.  After the K loop they move the
-//             fp32 accumulator TMEM -> shared memory (token-major);
+//   warp 1    allocates all 512 TMEM columns (two BT-column accumulators, one
+//             per 128-row half, + 4 A stages of 64 columns); one thread issues
+//             tcgen05.mma (kind::f16, M=128, N=BT, K=16; A = dequantized W from
+//             TMEM, B = x K-major from shared memory) and tcgen05.commit;
+//   warps 4-19 dequantize: warp group g = (row half, k half) owns rows
+//             [128*(g>>1), +128) and k [32*(g&1), +32) of every stage, thread t
+//             of the group weight row t = TMEM lane t; codes become bf16
+//             scale*q + bias stored with tcgen05.st straight into the A stage
+//             (row = lane, two k per 32-bit column), so the weight operand never
+//             touches shared memory, whose bandwidth the x operand and the TMA
+//             writes need.  After the K loop they move the fp32 accumulator
+//             TMEM -> shared memory (token-major);
 //   all warps reduce the S splits and store bf16 y with coalesced 8-byte stores.
 // No multicast anywhere (this path may run in multi-GPU processes).
 #include <cooperative_groups.h>
@@ -33,14 +40,12 @@ namespace vmlx {
 
 int sm_count();
 
-constexpr int TC_BN = 128;  // weight rows per tile (UMMA M)
+constexpr int TC_UM = 128;  // UMMA M (weight rows per MMA = TMEM lanes)
+constexpr int TC_BN = 256;  // weight rows per tile (two MMA halves)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row of bf16)
-constexpr int TC_SX = 3;    // x stages
-constexpr int TC_SR = 4;    // raw W stages
-constexpr int TC_SA = 2;    // dequantized A stages
-constexpr int TC_WARPS = 12;
+constexpr int TC_WARPS = 20;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_DQ = 256;  // dequantizing threads (warps 4-11)
+constexpr int TC_DQ = 512;  // dequantizing threads (warps 4-19)
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   // start address >> 4 | LBO (unused for swizzled K-major, 1) | SBO = 1024 B between
@@ -51,20 +56,21 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 
 // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128.
 __host__ __device__ constexpr uint32_t tc_idesc(int bt) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bt >> 3) << 17) | ((uint32_t)(TC_BN >> 4) << 24);
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bt >> 3) << 17) | ((uint32_t)(TC_UM >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// A from tensor memory (row = lane, K-major, two bf16 per column), B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
@@ -76,6 +82,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 8 4-bit codes (one packed word, LSB first) -> 8 bf16 s*q + b, each rounded once.
 // Codes are made exact as bf16 128+q (high byte 0x43, q in the low mantissa bits).
@@ -107,17 +123,30 @@ __device__ __forceinline__ uint4 dq8_8bit(uint32_t w0, uint32_t w1, float s, flo
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Ring depths per token-tile width: enough bytes in flight per SM to cover the
+// L2/HBM latency of the TMA loads.  A raw W stage is one [256 rows x 128 B] box
+// with the 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)): it covers
+// RKS k-stages, keeps the TMA row-request count low, and a warp's 16-byte reads
+// of 32 consecutive rows are bank-conflict free.  Shared memory stays above half
+// the SM's, so one CTA owns the SM's 512 TMEM columns.
 template <int BITS, int BT>
 struct TcLayout {
-  static constexpr int RAWB = TC_BK * BITS / 8;  // packed bytes per weight row per stage
-  static constexpr int XS = BT * 128;            // x stage bytes
-  static constexpr int AS = TC_BN * 128;         // A stage bytes
-  static constexpr int RS = TC_BN * RAWB;        // raw stage bytes
-  static constexpr int RING = TC_SX * XS + TC_SA * AS + TC_SR * RS;
-  static constexpr int RED = BT * TC_BN * 4;     // fp32 accumulator, token-major
+  static constexpr int SX = BT == 128 ? 6 : 8;    // x stages
+  static constexpr int SR = 3;                    // raw W stages
+  static constexpr int SA = 4;                    // dequantized A stages (TMEM)
+  static constexpr int RAWB = TC_BK * BITS / 8;   // packed bytes per weight row per k-stage
+  static constexpr int RKS = 128 / RAWB;          // k-stages per raw stage
+  static constexpr int XS = BT * 128;             // x stage bytes
+  static constexpr int RS = TC_BN * 128;          // raw stage bytes
+  static constexpr int RING = SX * XS + SR * RS;
+  static constexpr int A_COL = 2 * BT;            // first TMEM column of the A stages
+  static constexpr int TCOLS = 512;
+  static_assert(A_COL + SA * 64 <= TCOLS, "TMEM budget");
+  static constexpr int RED = BT * TC_BN * 4;      // fp32 accumulator, token-major
   static constexpr int DATA = RING > RED ? RING : RED;
-  static constexpr int BARS = (2 * TC_SX + 2 * TC_SR + 2 * TC_SA + 1) * 8 + 16;
+  static constexpr int BARS = (2 * SX + 2 * SR + 2 * SA + 1) * 8 + 16;
   static constexpr size_t SMEM = (size_t)DATA + BARS + 1024;
+  static_assert(SMEM > 116 * 1024 && SMEM <= 227 * 1024, "one CTA per SM");
 };
 
 template <int BITS, int GS, int BT>
@@ -126,20 +155,20 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
               const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y,
               int M, int N, int K, int S, int* status) {
   using L = TcLayout<BITS, BT>;
+  constexpr int SX = L::SX, SA = L::SA, SR = L::SR;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
   uint8_t* xs = smem;
-  uint8_t* as = xs + TC_SX * L::XS;
-  uint8_t* raw = as + TC_SA * L::AS;
+  uint8_t* raw = xs + SX * L::XS;
   float* red = reinterpret_cast<float*>(smem);  // reuses the rings once the K loop is done
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::DATA);
   uint64_t* x_full = bars;
-  uint64_t* x_empty = x_full + TC_SX;
-  uint64_t* r_full = x_empty + TC_SX;
-  uint64_t* r_empty = r_full + TC_SR;
-  uint64_t* a_full = r_empty + TC_SR;
-  uint64_t* a_empty = a_full + TC_SA;
-  uint64_t* acc_full = a_empty + TC_SA;
+  uint64_t* x_empty = x_full + SX;
+  uint64_t* r_full = x_empty + SX;
+  uint64_t* r_empty = r_full + SR;
+  uint64_t* a_full = r_empty + SR;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* acc_full = a_empty + SA;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -150,9 +179,9 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   const int KG = K / GS;
 
   if (tid == 0) {
-    for (int i = 0; i < TC_SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-    for (int i = 0; i < TC_SR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], TC_DQ / 32); }
-    for (int i = 0; i < TC_SA; i++) { mbar_init(&a_full[i], TC_DQ / 32); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < SX; i++) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < SR; i++) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], TC_DQ / 32); }
+    for (int i = 0; i < SA; i++) { mbar_init(&a_full[i], TC_DQ / 32); mbar_init(&a_empty[i], 1); }
     mbar_init(acc_full, 1);
     fence_mbar_init();
   }
@@ -162,7 +191,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BT));
+                 "r"(L::TCOLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   // Setup above overlaps the previous kernel's tail under programmatic launch; from here on
@@ -178,11 +207,14 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < nkb; i++) {
-        const int kb = kb0 + i, sx = i % TC_SX, sr = i % TC_SR;
-        if (i >= TC_SR) ok &= mbar_wait(&r_empty[sr], ((i / TC_SR) - 1) & 1);
-        mbar_arrive_expect_tx(&r_full[sr], L::RS);
-        tma_load_2d(raw + (size_t)sr * L::RS, &tmw, kb * L::RAWB, n0, &r_full[sr]);
-        if (i >= TC_SX) ok &= mbar_wait(&x_empty[sx], ((i / TC_SX) - 1) & 1);
+        const int kb = kb0 + i, sx = i % SX;
+        if (i % L::RKS == 0) {  // raw stage j covers k-stages [j*RKS, j*RKS + RKS) of this split
+          const int j = i / L::RKS, sr = j % SR;
+          if (j >= SR) ok &= mbar_wait(&r_empty[sr], ((j / SR) - 1) & 1);
+          mbar_arrive_expect_tx(&r_full[sr], L::RS);
+          tma_load_2d(raw + (size_t)sr * L::RS, &tmw, kb * L::RAWB, n0, &r_full[sr]);
+        }
+        if (i >= SX) ok &= mbar_wait(&x_empty[sx], ((i / SX) - 1) & 1);
         mbar_arrive_expect_tx(&x_full[sx], L::XS);
         tma_load_2d(xs + (size_t)sx * L::XS, &tmx, kb * TC_BK, m0, &x_full[sx]);
       }
@@ -191,70 +223,97 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
     if (lane == 0) {
       constexpr uint32_t idesc = tc_idesc(BT);
       for (int i = 0; i < nkb; i++) {
-        const int sx = i % TC_SX, sa = i % TC_SA;
-        ok &= mbar_wait(&a_full[sa], (i / TC_SA) & 1);
-        ok &= mbar_wait(&x_full[sx], (i / TC_SX) & 1);
+        const int sx = i % SX, sa = i % SA;
+        ok &= mbar_wait(&a_full[sa], (i / SA) & 1);
+        ok &= mbar_wait(&x_full[sx], (i / SX) & 1);
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(as + (size_t)sa * L::AS);
+        const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL + sa * 64);
         const uint32_t b_addr = smem_u32(xs + (size_t)sx * L::XS);
 #pragma unroll
-        for (int k = 0; k < TC_BK / 16; k++)
-          umma_f16(tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
-                   (i | k) ? 1u : 0u);
+        for (int k = 0; k < TC_BK / 16; k++) {
+          const uint64_t db = umma_desc_sw128(b_addr + k * 32);
+#pragma unroll
+          for (int mh = 0; mh < 2; mh++)
+            umma_f16_ts(tmem + (uint32_t)(mh * BT), a_tmem + mh * 32 + k * 8, db, idesc, (i | k) ? 1u : 0u);
+        }
         umma_commit(&a_empty[sa]);
         umma_commit(&x_empty[sx]);
       }
       umma_commit(acc_full);
     }
   } else if (warp >= 4) {
-    // ---------------- dequantize W into the SW128 A tile ----------------
+    // ---------------- dequantize W into the TMEM A stages ----------------
     const int dq = tid - 128;
-    const int h = dq >> 7;   // k half of the stage
-    const int r = dq & 127;  // weight row within the tile
-    const int row = n0 + r < N ? n0 + r : N - 1;
+    const int g = dq >> 7;     // warp group: row half g >> 1, k half g & 1
+    const int mh = g >> 1, h = g & 1;
+    const int r = dq & 127;    // row within the half = TMEM lane
+    const int q4 = warp & 3;   // this warp's TMEM lane quarter: r == 32*q4 + lane
+    const int rt = mh * TC_UM + r;  // row within the tile
+    const int row = n0 + rt < N ? n0 + rt : N - 1;
     const bf16* srow = scales + (int64_t)row * KG;
     const bf16* brow = biases + (int64_t)row * KG;
+    // group of this thread's 32 k in stage i (32 k never straddle a group, GS >= 32);
+    // loaded one stage ahead
+    auto grp = [&](int i) { return ((kb0 + i) * TC_BK + h * 32) / GS; };
+    bf16 sn = srow[grp(0)], bn = brow[grp(0)];
     for (int i = 0; i < nkb; i++) {
-      const int kb = kb0 + i, sr = i % TC_SR, sa = i % TC_SA;
-      const int g = (kb * TC_BK + h * 32) / GS;  // 32 k never straddle a group (GS >= 32)
-      const bf16 sv = srow[g], bv = brow[g];
-      ok &= mbar_wait(&r_full[sr], (i / TC_SR) & 1);
-      const uint8_t* rp = raw + (size_t)sr * L::RS + r * L::RAWB + h * (L::RAWB / 2);
-      uint32_t wv[BITS];  // this half's 32 codes: 4 words (4-bit) or 8 words (8-bit)
+      const int j = i / L::RKS, sub = i % L::RKS, sr = j % SR, sa = i % SA;
+      const bf16 sv = sn, bv = bn;
+      if (i + 1 < nkb) {
+        sn = srow[grp(i + 1)];
+        bn = brow[grp(i + 1)];
+      }
+      if (sub == 0) ok &= mbar_wait(&r_full[sr], (j / SR) & 1);
+      // this thread's 32 codes: 16-byte chunks c0 .. c0 + BITS/4 of its row (4 words for 4-bit, 8 for 8-bit)
+      const uint8_t* rp = raw + (size_t)sr * L::RS + rt * 128;
+      const int c0 = (sub * L::RAWB + h * (L::RAWB / 2)) >> 4;
+      uint32_t wv[BITS];
 #pragma unroll
       for (int v = 0; v < BITS / 4; v++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(rp + v * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(rp + (((c0 + v) ^ (rt & 7)) << 4));
         wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&r_empty[sr]);
-      if (i >= TC_SA) ok &= mbar_wait(&a_empty[sa], ((i / TC_SA) - 1) & 1);
-      uint8_t* arow = as + (size_t)sa * L::AS + r * 128;
+      if (sub == L::RKS - 1 || i == nkb - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r_empty[sr]);
+      }
+      uint32_t o[16];
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        const int chunk = h * 4 + c;  // 8 bf16 = 16 bytes; stored at (chunk ^ (r & 7)) (128-byte swizzle)
-        uint4 o;
+        uint4 q;
         if constexpr (BITS == 4) {
-          o = dq8_4bit(wv[c], __bfloat162bfloat162(sv), __bfloat162bfloat162(bv));
+          q = dq8_4bit(wv[c], __bfloat162bfloat162(sv), __bfloat162bfloat162(bv));
         } else {
-          o = dq8_8bit(wv[2 * c], wv[2 * c + 1], __bfloat162float(sv), __bfloat162float(bv));
+          q = dq8_8bit(wv[2 * c], wv[2 * c + 1], __bfloat162float(sv), __bfloat162float(bv));
         }
-        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = o;
+        o[4 * c] = q.x; o[4 * c + 1] = q.y; o[4 * c + 2] = q.z; o[4 * c + 3] = q.w;
       }
-      fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+      // Publish the previous stage: its TMEM store overlapped this stage's loads and math.
+      if (i > 0) {
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[(i - 1) % SA]);
+      }
+      if (i >= SA) ok &= mbar_wait(&a_empty[sa], ((i / SA) - 1) & 1);
+      tc_fence_after();
+      // A stage sa, half mh: lane = row, columns [h*16, h*16+16) hold k [32h, 32h+32) in pairs
+      tmem_st16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(L::A_COL + sa * 64 + mh * 32 + h * 16), o);
+    }
+    if (nkb > 0) {
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[sa]);
+      if (lane == 0) mbar_arrive(&a_full[(nkb - 1) % SA]);
     }
     // ---------------- accumulator: TMEM -> shared memory (token-major) ----------------
     ok &= mbar_wait(acc_full, 0);
     tc_fence_after();
-    const int q4 = warp & 3;  // TMEM lanes 32*q4 .. +31 = weight rows
-    const int rr = q4 * 32 + lane;
     for (int c0 = h * (BT / 2); c0 < (h + 1) * (BT / 2); c0 += 16) {
       uint32_t v[16];
-      tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+      tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mh * BT + c0), v);
 #pragma unroll
-      for (int j = 0; j < 16; j++) red[(c0 + j) * TC_BN + rr] = __uint_as_float(v[j]);
+      for (int j = 0; j < 16; j++) red[(c0 + j) * TC_BN + rt] = __uint_as_float(v[j]);
     }
   }
   tc_fence_before();
@@ -267,26 +326,31 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   // ---------------- reduce the splits (fixed order) and store bf16 y ----------------
   {
     const int t_lo = split * BT / S, t_hi = (split + 1) * BT / S;
-    const int n = n0 + 4 * lane;
-    const bool vec = (N & 3) == 0 && n + 4 <= N;
+    const int n = n0 + 8 * lane;
+    const bool vec = (N & 7) == 0 && n + 8 <= N;
     cg::cluster_group cluster = cg::this_cluster();
     for (int t = t_lo + warp; t < t_hi; t += TC_WARPS) {
       const int m = m0 + t;
       if (m >= M) break;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int q = 0; q < S; q++) {
-        const float* src = S > 1 ? cluster.map_shared_rank(red, q) : red;
-        const float4 v = *reinterpret_cast<const float4*>(src + t * TC_BN + 4 * lane);
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        const float* src = (S > 1 ? cluster.map_shared_rank(red, q) : red) + t * TC_BN + 8 * lane;
+        const float4 v0 = *reinterpret_cast<const float4*>(src);
+        const float4 v1 = *reinterpret_cast<const float4*>(src + 4);
+        acc[0] += v0.x; acc[1] += v0.y; acc[2] += v0.z; acc[3] += v0.w;
+        acc[4] += v1.x; acc[5] += v1.y; acc[6] += v1.z; acc[7] += v1.w;
       }
       bf16* yr = y + (int64_t)m * N;
       if (vec) {
-        const bf162 a = __floats2bfloat162_rn(acc.x, acc.y), b = __floats2bfloat162_rn(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(yr + n) = make_uint2(bf162_as_u32(a), bf162_as_u32(b));
+        uint4 o;
+        o.x = bf162_as_u32(__floats2bfloat162_rn(acc[0], acc[1]));
+        o.y = bf162_as_u32(__floats2bfloat162_rn(acc[2], acc[3]));
+        o.z = bf162_as_u32(__floats2bfloat162_rn(acc[4], acc[5]));
+        o.w = bf162_as_u32(__floats2bfloat162_rn(acc[6], acc[7]));
+        *reinterpret_cast<uint4*>(yr + n) = o;
       } else {
-        const float e[4] = {acc.x, acc.y, acc.z, acc.w};
-        for (int j = 0; j < 4; j++)
-          if (n + j < N) yr[n + j] = __float2bfloat16_rn(e[j]);
+        for (int j = 0; j < 8; j++)
+          if (n + j < N) yr[n + j] = __float2bfloat16_rn(acc[j]);
       }
     }
   }
@@ -295,7 +359,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
     cluster_wait();
   }
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TCOLS));
   if (!ok && status) atomicExch(status, VMLX_E_STATE);
 }
 
@@ -315,7 +379,7 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
   if (!make_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TC_BK,
                     BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K * BITS / 8, (uint64_t)N,
-                    (uint64_t)K * BITS / 8, L::RAWB, TC_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                    (uint64_t)K * BITS / 8, 128, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return VMLX_E_CUDA;
   // K splits: fill the SMs when the tile grid is small; each split keeps >= 8 stages.
   const int64_t ntn = (N + TC_BN - 1) / TC_BN, ntm = (M + BT - 1) / BT;
@@ -344,9 +408,6 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
 template <int BITS, int GS>
 static int launch_bt(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int64_t M, int64_t N,
                      int64_t K, cudaStream_t st) {
-  // 256-token tiles halve the dequantization per flop once M fills them and the grid stays wide
-  if (M > 128 && ((N + TC_BN - 1) / TC_BN) * ((M + 255) / 256) >= sm_count() / 2)
-    return launch_tc<BITS, GS, 256>(x, w, s, b, y, M, N, K, st);
   if (M > 64) return launch_tc<BITS, GS, 128>(x, w, s, b, y, M, N, K, st);
   return launch_tc<BITS, GS, 64>(x, w, s, b, y, M, N, K, st);
 }
