@@ -6,19 +6,18 @@
 // QuantizedBlockLoader / dequantize, :525-739) and multiplied on the matrix
 // units with fp32 accumulation.
 //
-// One CTA computes a 256 (weight rows) x BT (tokens) tile of y^T over one K
+// One CTA computes a BN (128 or 256 weight rows: one or two M=128 MMA halves
+// sharing each x stage) x BT (64, 128 or 256 tokens) tile of y^T over one K
 // split; S > 1 splits of a tile form a thread-block cluster and reduce through
-// distributed shared memory in a fixed order (deterministic).  Every weight
-// tile streams all of x from L2, so x traffic per flop falls as 1/rows-per-tile:
-// 256 rows (two M=128 MMAs sharing each x stage) keep it inside L2 bandwidth.
+// distributed shared memory in a fixed order (deterministic).
 //   warp 0    TMA producer: x tile [BT tokens x 64 k] (128-byte swizzle = the
-//             UMMA K-major SW128 layout) and the raw packed W tile [256 rows x
-//             64 k] into rings completing on mbarriers;
-//   warp 1    allocates all 512 TMEM columns (two BT-column accumulators, one
-//             per 128-row half, + 4 A stages of 64 columns); one thread issues
+//             UMMA K-major SW128 layout) and the raw packed W tile [BN rows x
+//             128 B] into rings completing on mbarriers;
+//   warp 1    allocates TMEM (a BT-column accumulator per 128-row half + 4 A
+//             stages of 32 columns per half); one thread issues
 //             tcgen05.mma (kind::f16, M=128, N=BT, K=16; A = dequantized W from
 //             TMEM, B = x K-major from shared memory) and tcgen05.commit;
-//   warps 4-19 dequantize: warp group g = (row half, k half) owns rows
+//   warps 4.. dequantize: warp group g = (row half, k half) owns rows
 //             [128*(g>>1), +128) and k [32*(g&1), +32) of every stage, thread t
 //             of the group weight row t = TMEM lane t; codes become bf16
 //             scale*q + bias stored with tcgen05.st straight into the A stage
@@ -41,11 +40,7 @@ namespace vmlx {
 int sm_count();
 
 constexpr int TC_UM = 128;  // UMMA M (weight rows per MMA = TMEM lanes)
-constexpr int TC_BN = 256;  // weight rows per tile (two MMA halves)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row of bf16)
-constexpr int TC_WARPS = 20;
-constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_DQ = 512;  // dequantizing threads (warps 4-19)
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   // start address >> 4 | LBO (unused for swizzled K-major, 1) | SBO = 1024 B between
@@ -129,33 +124,41 @@ __device__ __forceinline__ uint4 dq8_8bit(uint32_t w0, uint32_t w1, float s, flo
 // RKS k-stages, keeps the TMA row-request count low, and a warp's 16-byte reads
 // of 32 consecutive rows are bank-conflict free.  Shared memory stays above half
 // the SM's, so one CTA owns the SM's 512 TMEM columns.
-template <int BITS, int BT>
+// NH = 128-row MMA halves per tile (tile rows BN = 128*NH).  Warps: 0 producer, 1 MMA,
+// 2-3 idle, then 8*NH dequantizing warps (NH row halves x 2 k halves x 4 lane quarters).
+template <int BITS, int BT, int NH>
 struct TcLayout {
-  static constexpr int SX = BT == 128 ? 6 : 8;    // x stages
+  static constexpr int BN = TC_UM * NH;           // weight rows per tile
+  static constexpr int DQ = 256 * NH;             // dequantizing threads
+  static constexpr int WARPS = 4 + DQ / 32;
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int SX = BT == 256 ? 4 : BT == 128 ? 6 : 8;  // x stages
   static constexpr int SR = 3;                    // raw W stages
   static constexpr int SA = 4;                    // dequantized A stages (TMEM)
   static constexpr int RAWB = TC_BK * BITS / 8;   // packed bytes per weight row per k-stage
   static constexpr int RKS = 128 / RAWB;          // k-stages per raw stage
   static constexpr int XS = BT * 128;             // x stage bytes
-  static constexpr int RS = TC_BN * 128;          // raw stage bytes
+  static constexpr int RS = BN * 128;             // raw stage bytes
   static constexpr int RING = SX * XS + SR * RS;
-  static constexpr int A_COL = 2 * BT;            // first TMEM column of the A stages
-  static constexpr int TCOLS = 512;
-  static_assert(A_COL + SA * 64 <= TCOLS, "TMEM budget");
-  static constexpr int RED = BT * TC_BN * 4;      // fp32 accumulator, token-major
+  static constexpr int A_COL = NH * BT;           // first TMEM column of the A stages
+  static constexpr int A_W = NH * 32;             // TMEM columns per A stage
+  static constexpr int TCOLS = A_COL + SA * A_W <= 256 ? 256 : 512;
+  static_assert(A_COL + SA * A_W <= 512, "TMEM budget");
+  static constexpr int RED = BT * BN * 4;         // fp32 accumulator, token-major
   static constexpr int DATA = RING > RED ? RING : RED;
   static constexpr int BARS = (2 * SX + 2 * SR + 2 * SA + 1) * 8 + 16;
   static constexpr size_t SMEM = (size_t)DATA + BARS + 1024;
-  static_assert(SMEM > 116 * 1024 && SMEM <= 227 * 1024, "one CTA per SM");
+  // a CTA holding all 512 TMEM columns must own its SM: more than half the shared memory
+  static_assert(SMEM <= 227 * 1024 && (TCOLS == 256 || SMEM > 116 * 1024), "one CTA per SM");
 };
 
-template <int BITS, int GS, int BT>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int BITS, int GS, int BT, int NH>
+__global__ void __launch_bounds__(TcLayout<BITS, BT, NH>::THREADS, 1)
 qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
               const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y,
               int M, int N, int K, int S, int* status) {
-  using L = TcLayout<BITS, BT>;
-  constexpr int SX = L::SX, SA = L::SA, SR = L::SR;
+  using L = TcLayout<BITS, BT, NH>;
+  constexpr int SX = L::SX, SA = L::SA, SR = L::SR, TC_BN = L::BN, TC_DQ = L::DQ, TC_WARPS = L::WARPS;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   uint8_t* smem = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
   uint8_t* xs = smem;
@@ -227,13 +230,13 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
         ok &= mbar_wait(&a_full[sa], (i / SA) & 1);
         ok &= mbar_wait(&x_full[sx], (i / SX) & 1);
         tc_fence_after();
-        const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL + sa * 64);
+        const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL + sa * L::A_W);
         const uint32_t b_addr = smem_u32(xs + (size_t)sx * L::XS);
 #pragma unroll
         for (int k = 0; k < TC_BK / 16; k++) {
           const uint64_t db = umma_desc_sw128(b_addr + k * 32);
 #pragma unroll
-          for (int mh = 0; mh < 2; mh++)
+          for (int mh = 0; mh < NH; mh++)
             umma_f16_ts(tmem + (uint32_t)(mh * BT), a_tmem + mh * 32 + k * 8, db, idesc, (i | k) ? 1u : 0u);
         }
         umma_commit(&a_empty[sa]);
@@ -298,7 +301,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
       if (i >= SA) ok &= mbar_wait(&a_empty[sa], ((i / SA) - 1) & 1);
       tc_fence_after();
       // A stage sa, half mh: lane = row, columns [h*16, h*16+16) hold k [32h, 32h+32) in pairs
-      tmem_st16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(L::A_COL + sa * 64 + mh * 32 + h * 16), o);
+      tmem_st16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(L::A_COL + sa * L::A_W + mh * 32 + h * 16), o);
     }
     if (nkb > 0) {
       tmem_st_wait();
@@ -326,30 +329,33 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   // ---------------- reduce the splits (fixed order) and store bf16 y ----------------
   {
     const int t_lo = split * BT / S, t_hi = (split + 1) * BT / S;
-    const int n = n0 + 8 * lane;
-    const bool vec = (N & 7) == 0 && n + 8 <= N;
+    constexpr int NPL = TC_BN / 32;  // output columns per lane (4 or 8)
+    const int n = n0 + NPL * lane;
+    const bool vec = (N % NPL) == 0 && n + NPL <= N;
     cg::cluster_group cluster = cg::this_cluster();
     for (int t = t_lo + warp; t < t_hi; t += TC_WARPS) {
       const int m = m0 + t;
       if (m >= M) break;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float acc[NPL];
+#pragma unroll
+      for (int j = 0; j < NPL; j++) acc[j] = 0.f;
       for (int q = 0; q < S; q++) {
-        const float* src = (S > 1 ? cluster.map_shared_rank(red, q) : red) + t * TC_BN + 8 * lane;
-        const float4 v0 = *reinterpret_cast<const float4*>(src);
-        const float4 v1 = *reinterpret_cast<const float4*>(src + 4);
-        acc[0] += v0.x; acc[1] += v0.y; acc[2] += v0.z; acc[3] += v0.w;
-        acc[4] += v1.x; acc[5] += v1.y; acc[6] += v1.z; acc[7] += v1.w;
+        const float* src = (S > 1 ? cluster.map_shared_rank(red, q) : red) + t * TC_BN + NPL * lane;
+#pragma unroll
+        for (int j = 0; j < NPL; j += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src + j);
+          acc[j] += v.x; acc[j + 1] += v.y; acc[j + 2] += v.z; acc[j + 3] += v.w;
+        }
       }
       bf16* yr = y + (int64_t)m * N;
       if (vec) {
-        uint4 o;
-        o.x = bf162_as_u32(__floats2bfloat162_rn(acc[0], acc[1]));
-        o.y = bf162_as_u32(__floats2bfloat162_rn(acc[2], acc[3]));
-        o.z = bf162_as_u32(__floats2bfloat162_rn(acc[4], acc[5]));
-        o.w = bf162_as_u32(__floats2bfloat162_rn(acc[6], acc[7]));
-        *reinterpret_cast<uint4*>(yr + n) = o;
+        uint32_t o[NPL / 2];
+#pragma unroll
+        for (int j = 0; j < NPL / 2; j++) o[j] = bf162_as_u32(__floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]));
+        if constexpr (NPL == 8) *reinterpret_cast<uint4*>(yr + n) = make_uint4(o[0], o[1], o[2], o[3]);
+        else *reinterpret_cast<uint2*>(yr + n) = make_uint2(o[0], o[1]);
       } else {
-        for (int j = 0; j < 8; j++)
+        for (int j = 0; j < NPL; j++)
           if (n + j < N) yr[n + j] = __float2bfloat16_rn(acc[j]);
       }
     }
@@ -363,11 +369,11 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
   if (!ok && status) atomicExch(status, VMLX_E_STATE);
 }
 
-template <int BITS, int GS, int BT>
+template <int BITS, int GS, int BT, int NH>
 static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y, int64_t M,
                      int64_t N, int64_t K, cudaStream_t st) {
-  using L = TcLayout<BITS, BT>;
-  auto kern = qmm_tc_kernel<BITS, GS, BT>;
+  using L = TcLayout<BITS, BT, NH>;
+  auto kern = qmm_tc_kernel<BITS, GS, BT, NH>;
   static bool attr = false;
   if (!attr) {
     int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM),
@@ -379,16 +385,17 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
   if (!make_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TC_BK,
                     BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K * BITS / 8, (uint64_t)N,
-                    (uint64_t)K * BITS / 8, 128, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B))
+                    (uint64_t)K * BITS / 8, 128, L::BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return VMLX_E_CUDA;
-  // K splits: fill the SMs when the tile grid is small; each split keeps >= 8 stages.
-  const int64_t ntn = (N + TC_BN - 1) / TC_BN, ntm = (M + BT - 1) / BT;
+  // K splits fill the SMs when the tile grid is small; each split keeps >= 8 stages, and
+  // clusters stay at <= 4 CTAs so that they co-schedule in one wave.
+  const int64_t ntn = (N + L::BN - 1) / L::BN, ntm = (M + BT - 1) / BT;
   const int64_t tiles = ntn * ntm, KB = K / TC_BK;
   int S = 1;
-  while (S < 8 && tiles * S * 2 <= sm_count() && KB / (S * 2) >= 8) S *= 2;
+  while (S < 4 && tiles * S * 2 <= sm_count() && KB / (S * 2) >= 8) S *= 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(ntn * S), (unsigned)ntm, 1);
-  cfg.blockDim = dim3(TC_THREADS);
+  cfg.blockDim = dim3(L::THREADS);
   cfg.dynamicSmemBytes = L::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attrs[2];
@@ -405,11 +412,22 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
                     "qmm_tc_kernel launch");
 }
 
+// Tile shape by problem shape (measured on B200, 4-bit g64 Llama FFN shapes):
+//   - many token tiles: 128 weight rows x 256 tokens (least dequantization per flop);
+//   - otherwise 256 weight rows (two MMA halves sharing each x stage) when that still
+//     gives >= 56 tiles, else 128 rows with K splits.
 template <int BITS, int GS>
 static int launch_bt(const bf16* x, const uint32_t* w, const bf16* s, const bf16* b, bf16* y, int64_t M, int64_t N,
                      int64_t K, cudaStream_t st) {
-  if (M > 64) return launch_tc<BITS, GS, 128>(x, w, s, b, y, M, N, K, st);
-  return launch_tc<BITS, GS, 64>(x, w, s, b, y, M, N, K, st);
+  const int64_t sms = sm_count();
+  const int64_t ntn1 = (N + 127) / 128, ntn2 = (N + 255) / 256;
+  if (M > 128 && ntn1 * ((M + 255) / 256) >= sms / 2) return launch_tc<BITS, GS, 256, 1>(x, w, s, b, y, M, N, K, st);
+  if (M > 64) {
+    if (ntn2 * ((M + 127) / 128) >= 56) return launch_tc<BITS, GS, 128, 2>(x, w, s, b, y, M, N, K, st);
+    return launch_tc<BITS, GS, 128, 1>(x, w, s, b, y, M, N, K, st);
+  }
+  if (ntn2 >= 56) return launch_tc<BITS, GS, 64, 2>(x, w, s, b, y, M, N, K, st);
+  return launch_tc<BITS, GS, 64, 1>(x, w, s, b, y, M, N, K, st);
 }
 
 int launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y, int64_t M,
