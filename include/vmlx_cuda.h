@@ -253,6 +253,24 @@ VMLX_API int vmlx_tp_set_timeout_us(void* tp, uint64_t us);
 VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, void* stream);
 
 /*
+ * Row-parallel quantized linear fused with its all-reduce and the residual add
+ * (decode, 1 <= M <= 32, M*N*2 <= max_bytes):
+ *   y[M, N] = bf16(residual + bf16(sum_r x_r[M, K] @ dequantize(w_r[N, K])^T))
+ * where rank r holds the K-shard x_r / w_r (scales / biases [N, K/group_size]).
+ * Replaces QuantizedShardedToAllLinear.callAsFunction -> Collectives.allSum
+ * (Libraries/MLXDistributedTP/LinearLayers.swift:198-205, Collectives.swift:27-32)
+ * plus the decoder residual add (Libraries/MLXLLM/Models/Llama.swift:110-114).
+ * One kernel per rank: the GEMV pushes its bf16 partial rows into every rank's
+ * slot over NVLink P2P; each CTA then waits (bounded) for the same CTA of every
+ * rank and sums its rows in rank order -- bitwise equal to quantized_matmul,
+ * vmlx_tp_all_sum and add run separately.  residual may be NULL or alias y.
+ * Every rank must make the same sequence of calls.  Size 1: the local fused GEMV.
+ */
+VMLX_API int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x, const uint32_t* w,
+                                              const void* scales, const void* biases, int group_size, int bits,
+                                              int64_t M, int64_t N, int64_t K, const void* residual, void* stream);
+
+/*
  * Reads (synchronously) and clears the group's device status word:
  * *code = 0, or VMLX_E_PEER_TIMEOUT if some wait on a peer ran out since the
  * last read.

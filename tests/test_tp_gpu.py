@@ -56,6 +56,42 @@ def test_peer_timeout_sets_status_and_context_survives(vm, cuda):
     lib.vmlx_tp_destroy(h1)
 
 
+def test_fused_tp_linear_size1_and_timeout(vm, cuda):
+    """world 1: the fused TP linear is the local fused GEMV (+ residual).  world 2 with a
+    rank that never runs: every CTA's bounded wait gives up, the status reports it, y is
+    left untouched and the context stays usable."""
+    lib = vm.lib()
+    g = torch.Generator(cuda).manual_seed(4)
+    K, N, M = 2048, 1024, 3
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+    wq, s, b = vm.quantized(w)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+    h = ctypes.c_void_p()
+    assert lib.vmlx_tp_create(0, 1, 1 << 20, ctypes.byref(h)) == 0
+    y = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    assert lib.vmlx_tp_quantized_matmul_all_sum(h, y.data_ptr(), x.data_ptr(), wq.data_ptr(), s.data_ptr(),
+                                                b.data_ptr(), 64, 4, M, N, K, res.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y, vm.ops.quantized_mm_fused(x, wq, s, b, residual=res))
+    lib.vmlx_tp_destroy(h)
+    h0, h1 = ctypes.c_void_p(), ctypes.c_void_p()
+    assert lib.vmlx_tp_create(0, 2, 1 << 20, ctypes.byref(h0)) == 0
+    assert lib.vmlx_tp_create(1, 2, 1 << 20, ctypes.byref(h1)) == 0
+    assert lib.vmlx_tp_set_peer(h0, 1, lib.vmlx_tp_buffer(h1)) == 0
+    assert lib.vmlx_tp_set_timeout_us(h0, 20000) == 0
+    y.zero_()
+    assert lib.vmlx_tp_quantized_matmul_all_sum(h0, y.data_ptr(), x.data_ptr(), wq.data_ptr(), s.data_ptr(),
+                                                b.data_ptr(), 64, 4, M, N, K, res.data_ptr(), None) == 0
+    code = ctypes.c_int(-1)
+    assert lib.vmlx_tp_status(h0, ctypes.byref(code)) == 0
+    assert code.value == vm._lib.VMLX_E_PEER_TIMEOUT
+    assert torch.count_nonzero(y) == 0
+    assert (x.float() * 2).sum().isfinite().item()
+    lib.vmlx_tp_destroy(h0)
+    lib.vmlx_tp_destroy(h1)
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -109,9 +145,45 @@ def _tp_worker(rank, world, port, q):
             tp.k_cache[i].copy_(full.k_cache[i][:, rank * hk:(rank + 1) * hk])
             tp.v_cache[i].copy_(full.v_cache[i][:, rank * hk:(rank + 1) * hk])
         y1 = full.step(x0.clone(), 32).float()
+        caches = [(k.clone(), v.clone()) for k, v in zip(tp.k_cache, tp.v_cache)]
         yp = tp.step(x0.clone(), 32).float()
         rel = ((yp - y1).abs().max() / y1.abs().max()).item()
         ok.append(rel <= 2e-2)
+        # the same TP step with o_proj / down_proj as fused GEMV + all-reduce + residual kernels
+        tpf = vm.llama.LlamaDecoder(cfg, 2, max_len=48, dev=dev, seed=3, rank=rank, world=world, group=grp,
+                                    cache_fill=32)
+        for i in range(cfg.n_layers):
+            tpf.k_cache[i].copy_(caches[i][0])
+            tpf.v_cache[i].copy_(caches[i][1])
+        ypf = tpf.step(x0.clone(), 32).float()
+        ok.append(torch.equal(ypf, yp))  # same kernels up to the fused collective: bitwise equal
+        # fused row-parallel linear == partial GEMV -> all_sum -> add, bitwise, over graph replays
+        K, N = 1024, 512
+        wfull = (torch.randn(N, K, generator=torch.Generator().manual_seed(11)) * 0.02).bfloat16().to(dev)
+        ql = vm.llama.QuantLinear(*vm.quantized(wfull), 64, 4)
+        row = vm.distributed.QuantizedShardedToAllLinear(ql, grp)
+        for M in (1, 4, 9, 32):
+            xf = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).bfloat16().to(dev)
+            xl = xf[:, rank * K // world:(rank + 1) * K // world].contiguous()
+            res = torch.randn(M, N, generator=torch.Generator().manual_seed(50 + M)).bfloat16().to(dev)
+            fused = row(xl, residual=res)
+            sep = row(xl, residual=res, fused=False)
+            ok.append(torch.equal(fused, sep))
+        st2 = torch.cuda.Stream(dev)
+        xl = torch.randn(4, K // world, generator=torch.Generator().manual_seed(rank)).bfloat16().to(dev)
+        with torch.cuda.stream(st2):
+            outb = torch.empty(4, N, dtype=torch.bfloat16, device=dev)
+            row(xl, out=outb)
+            st2.synchronize()
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=st2):
+                row(xl, out=outb)
+                row(xl, residual=outb, out=outb)
+            for _ in range(4):
+                g2.replay()
+        torch.cuda.synchronize()
+        once = row(xl, fused=False)
+        ok.append(torch.equal(outb, vm.fast.add(once, once)))
         ok.append(grp.status() == 0)
         q.put((rank, ok, rel))
         grp.close()

@@ -66,6 +66,8 @@ SIGNATURES = {
     "vmlx_tp_buffer": (_vp, [_vp]),
     "vmlx_tp_set_timeout_us": (_int, [_vp, _c.c_uint64]),
     "vmlx_tp_all_sum": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "vmlx_tp_quantized_matmul_all_sum": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
+                                                _vp, _vp]),
     "vmlx_tp_status": (_int, [_vp, _c.POINTER(_int)]),
     "vmlx_tp_destroy": (_int, [_vp]),
 }

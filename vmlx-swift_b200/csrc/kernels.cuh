@@ -28,7 +28,19 @@ struct QmvArgs {
   const bf16* norm_w;   // x <- norm_w * bf16(x * rsqrt(mean(x^2) + eps)) over the full row
   float eps;
   const bf16* residual;  // y <- bf16(residual + bf16(x @ W^T)), residual laid out like y (may alias y)
+  // Row-parallel tensor parallelism (tp_world > 1, dense mode): the bf16 partial y of
+  // this rank goes into slot [parity][tp_rank] of every rank's buffer over P2P; each
+  // CTA then waits for the same CTA of every rank and reduces its rows in rank order:
+  //   y = bf16(residual + bf16(sum_r partial_r)).
+  char* tp_buf[8];  // every rank's TP buffer base, as seen from this device
+  int tp_rank, tp_world;
+  size_t tp_slot_bytes;                             // bytes per rank slot
+  size_t tp_slots_off, tp_flags_off, tp_epoch_off;  // regions inside each buffer
+  uint64_t tp_timeout_ns;
+  int* tp_status;  // set to VMLX_E_PEER_TIMEOUT when a peer wait runs out
 };
+
+constexpr int TP_FUSED_MAXC = 1024;  // CTAs of a fused TP GEMV grid (flag slots per rank)
 
 int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int toka, cudaStream_t st);
 

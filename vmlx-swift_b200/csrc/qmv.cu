@@ -158,8 +158,16 @@ __device__ __forceinline__ uint2 norm4(uint2 v, float inv, const bf16* w) {
   return make_uint2(o[0], o[1]);
 }
 
-// Store one output element, with the optional fused residual add.
-__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v) {
+// Store one output element, with the optional fused residual add.  Under row-parallel
+// TP the bf16 partial goes to slot [tpp][tp_rank] of every rank instead (P2P stores).
+__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v, int tpp) {
+  if (p.tp_world > 1) {
+    const bf16 hv = __float2bfloat16_rn(v);
+    const size_t off = p.tp_slots_off + ((size_t)tpp * p.tp_world + p.tp_rank) * p.tp_slot_bytes +
+                       (size_t)((yr - p.y) + col) * sizeof(bf16);
+    for (int r = 0; r < p.tp_world; r++) *reinterpret_cast<bf16*>(p.tp_buf[r] + off) = hv;
+    return;
+  }
   if (p.residual) {
     const bf16* rr = p.residual + (yr - p.y);
     const float s = __bfloat162float(__float2bfloat16_rn(v));
@@ -344,6 +352,18 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     // x and y may be produced / consumed by the previous kernel: wait for it
     // (a no-op unless this grid was launched with programmatic overlap).
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Row-parallel TP: this call's epoch (advanced by the grid's last CTA) picks the slot parity.
+    __shared__ uint32_t s_tp_e;
+    __shared__ int s_tp_ok;
+    if (p.tp_world > 1) {
+      if (tid == 0) {
+        s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off) + 1;
+        s_tp_ok = 1;
+      }
+      named_bar_sync(1, 32 * QMV_CWARPS);
+    }
+    const uint32_t tp_e = p.tp_world > 1 ? s_tp_e : 0u;
+    const int tpp = (int)(tp_e & 1);
     for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);
       if (I.ntok == 0) continue;
@@ -575,7 +595,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 const bf16* xr_unused;
                 bf16* yr;
                 token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-                store_y(p, yr, row, acc[t][j]);
+                store_y(p, yr, row, acc[t][j], tpp);
               }
             }
           }
@@ -684,7 +704,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                     const bf16* xr_unused;
                     bf16* yr;
                     token_rows(p, mode, I.base, chunk + t, xr_unused, yr);
-                    store_y(p, yr, I.n0 + r, res[j][t]);
+                    store_y(p, yr, I.n0 + r, res[j][t], tpp);
                   }
                 } else {
                   rb[r * TOKA + t] = res[j][t];
@@ -705,7 +725,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
               const bf16* xr_unused;
               bf16* yr;
               token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-              store_y(p, yr, I.n0 + r, s);
+              store_y(p, yr, I.n0 + r, s, tpp);
             }
           }
           red_count++;
@@ -714,6 +734,51 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
       if (!I.zero_rows && sc_tma) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&scempty[slot_sc]);
+      }
+    }
+    if (p.tp_world > 1) {
+      // ---- row-parallel all-reduce: publish, wait for the same CTA of every rank, reduce ----
+      auto flag = [&](int on_rank, int src) {
+        return reinterpret_cast<uint32_t*>(p.tp_buf[on_rank] + p.tp_flags_off) +
+               ((size_t)tpp * p.tp_world + src) * TP_FUSED_MAXC + blockIdx.x;
+      };
+      named_bar_sync(1, 32 * QMV_CWARPS);  // every partial store of this CTA is issued
+      if (tid < p.tp_world) {
+        __threadfence_system();
+        st_release_sys(flag(tid, p.tp_rank), tp_e);
+        if (!wait_flag_sys(flag(p.tp_rank, tid), tp_e, p.tp_timeout_ns)) {
+          s_tp_ok = 0;
+          if (p.tp_status) atomicExch(p.tp_status, VMLX_E_PEER_TIMEOUT);
+        }
+      }
+      named_bar_sync(1, 32 * QMV_CWARPS);
+      if (s_tp_ok) {
+        const int rlo = C > 1 ? crow_lo : 0, rhi = C > 1 ? crow_hi : QMV_ROWS, nr = rhi - rlo;
+        for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
+          const QmvItem I = qmv_item(p, mode, item, rowtiles);
+          for (int64_t i = tid; i < (int64_t)nr * I.ntok; i += 32 * QMV_CWARPS) {
+            const int64_t row = I.n0 + rlo + i % nr, tok = i / nr;
+            if (row >= p.N) continue;
+            const int64_t idx = tok * p.N + row;
+            float sum = 0.f;  // rank order: identical on every rank
+            for (int r = 0; r < p.tp_world; r++)
+              sum += __bfloat162float(*reinterpret_cast<const bf16*>(
+                  p.tp_buf[p.tp_rank] + p.tp_slots_off + ((size_t)tpp * p.tp_world + r) * p.tp_slot_bytes +
+                  (size_t)idx * sizeof(bf16)));
+            const bf16 sb = __float2bfloat16_rn(sum);
+            p.y[idx] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + __bfloat162float(sb)) : sb;
+          }
+        }
+      }
+      named_bar_sync(1, 32 * QMV_CWARPS);
+      if (tid == 0) {  // the grid's last CTA advances the epoch for the next call
+        uint32_t* ep = reinterpret_cast<uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off);
+        __threadfence();
+        if (atomicAdd(ep + 1, 1u) == gridDim.x - 1) {
+          ep[1] = 0;
+          ep[0] = tp_e;
+          __threadfence();
+        }
       }
     }
     if (C > 1) {  // keep this CTA's shared memory alive until every peer has read it
@@ -772,6 +837,9 @@ static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   if (max_clusters < 1) max_clusters = 1;
   const int64_t n_clusters = n_items < max_clusters ? n_items : max_clusters;
 
+  if (a.tp_world > 1 && n_clusters * C > TP_FUSED_MAXC)
+    return set_error(VMLX_E_UNSUPPORTED, "tp: fused grid of %lld CTAs exceeds %d", (long long)(n_clusters * C),
+                     TP_FUSED_MAXC);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(n_clusters * C), 1, 1);
   cfg.blockDim = dim3(QMV_THREADS);

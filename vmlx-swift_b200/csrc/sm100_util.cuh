@@ -57,6 +57,30 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// System-scope publish / observe for flags written over NVLink P2P, and the
+// global nanosecond timer used to bound waits on peers.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait until *f - e >= 0 (wrapping 32-bit epochs); false once deadline_ns has passed.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t e, uint64_t timeout_ns) {
+  const uint64_t deadline = globaltimer() + timeout_ns;
+  for (uint32_t it = 0;; it++) {
+    if ((int32_t)(ld_acquire_sys(f) - e) >= 0) return true;
+    if ((it & 1023) == 1023 && globaltimer() > deadline) return false;
+  }
+}
+
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 

@@ -7,7 +7,8 @@
 //
 // Design (one process per GPU, or one process driving several GPUs):
 //  * Every rank owns one device buffer: [2 parities][world][max_bytes] receive
-//    slots, then [2][world][TP_MAX_CTAS] uint32 flags, then [TP_MAX_CTAS] epochs.
+//    slots, then [2][world][TP_MAX_CTAS] uint32 flags, then [TP_MAX_CTAS] epochs,
+//    then the same kind of region for the fused row-parallel GEMV (below).
 //    Peers map it with CUDA IPC (or get its pointer directly in one process).
 //  * all_sum is one kernel: CTA c takes chunk c of the vector, stores it into
 //    slot [parity][my_rank] of every rank's buffer (P2P stores over NVLink /
@@ -27,6 +28,7 @@
 #include <cstring>
 
 #include "kernels.cuh"
+#include "sm100_util.cuh"
 
 namespace vmlx {
 
@@ -61,20 +63,19 @@ __host__ __device__ inline size_t tp_flag_off(size_t max_bytes, int world) {
 __host__ __device__ inline size_t tp_epoch_off(size_t max_bytes, int world) {
   return tp_flag_off(max_bytes, world) + (size_t)2 * world * TP_MAX_CTAS * sizeof(uint32_t);
 }
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Region of the fused row-parallel GEMV + all-reduce (its own slots, so that its
+// parity never aliases the standalone all_sum's): [2][world][max_bytes] slots,
+// [2][world][TP_FUSED_MAXC] flags, then {epoch, finished-CTA counter}.
+inline size_t tp_fused_slots_off(size_t max_bytes, int world) {
+  return (tp_epoch_off(max_bytes, world) + TP_MAX_CTAS * sizeof(uint32_t) + 255) / 256 * 256;
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+inline size_t tp_fused_flags_off(size_t max_bytes, int world) {
+  return tp_fused_slots_off(max_bytes, world) + (size_t)2 * world * max_bytes;
 }
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+inline size_t tp_fused_epoch_off(size_t max_bytes, int world) {
+  return tp_fused_flags_off(max_bytes, world) + (size_t)2 * world * TP_FUSED_MAXC * sizeof(uint32_t);
 }
+inline size_t tp_total_bytes(size_t max_bytes, int world) { return tp_fused_epoch_off(max_bytes, world) + 256; }
 
 // One-shot all-reduce of n bf16 elements (n * 2 <= max_bytes, chunked over CTAs).
 __global__ void __launch_bounds__(TP_THREADS)
@@ -118,13 +119,7 @@ tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf
   if (threadIdx.x < world) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + tp_flag_off(max_bytes, world)) +
                         ((size_t)parity * world + threadIdx.x) * TP_MAX_CTAS + c;
-    const uint64_t deadline = globaltimer() + timeout_ns;
-    bool arrived = false;
-    for (uint32_t it = 0;; it++) {
-      if ((int32_t)(ld_acquire_sys(f) - e) >= 0) { arrived = true; break; }
-      if ((it & 1023) == 1023 && globaltimer() > deadline) break;
-    }
-    if (!arrived) {
+    if (!wait_flag_sys(f, e, timeout_ns)) {
       s_ok = 0;
       atomicExch(status, VMLX_E_PEER_TIMEOUT);
     }
@@ -164,7 +159,7 @@ extern "C" int vmlx_tp_create(int rank, int world, size_t max_bytes, void** out)
   h->max_bytes = max_bytes;
   h->timeout_ns = 2000000000ull;  // 2 s
   int rc = check_cuda(cudaGetDevice(&h->device), "tp_create: cudaGetDevice");
-  h->total_bytes = tp_epoch_off(max_bytes, world) + TP_MAX_CTAS * sizeof(uint32_t);
+  h->total_bytes = tp_total_bytes(max_bytes, world);
   if (!rc) rc = check_cuda(cudaMalloc(&h->local, h->total_bytes), "tp_create: cudaMalloc");
   if (!rc) rc = check_cuda(cudaMemset(h->local, 0, h->total_bytes), "tp_create: cudaMemset");
   if (!rc) rc = check_cuda(cudaMalloc(&h->status, sizeof(int)), "tp_create: cudaMalloc status");
@@ -264,6 +259,49 @@ extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, v
   tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
       peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
   return check_launch("tp_all_sum_kernel");
+}
+
+// Row-parallel quantized linear fused with its all-reduce (and the residual add):
+//   y = residual + all_sum(x_shard @ dequantize(w_shard)^T)
+// replacing QuantizedShardedToAllLinear.callAsFunction -> allSum
+// (Libraries/MLXDistributedTP/LinearLayers.swift:198-205, Collectives.swift:27-32) followed by
+// the decoder's residual add (Libraries/MLXLLM/Models/Llama.swift:110-114).  Decode sizes
+// (M <= 32): the GEMV pushes its bf16 partial rows straight into every rank's slot
+// over NVLink and reduces them in the same kernel.
+extern "C" int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x, const uint32_t* w,
+                                                const void* scales, const void* biases, int group_size, int bits,
+                                                int64_t M, int64_t N, int64_t K, const void* residual,
+                                                void* stream) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (M == 0 && N > 0 && K > 0) return VMLX_OK;
+  if (M < 1 || M > 32) return set_error(VMLX_E_UNSUPPORTED, "tp_quantized_matmul_all_sum: M=%lld (1..32)", (long long)M);
+  if ((size_t)M * N * 2 > h->max_bytes)
+    return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: %lld x %lld output exceeds the %zu-byte slots",
+                     (long long)M, (long long)N, h->max_bytes);
+  if (h->world == 1)
+    return vmlx_cuda_quantized_matmul_fused(y, x, w, scales, biases, group_size, bits, M, N, K, nullptr, 0.f, residual,
+                                            stream);
+  if (!h->connected) return set_error(VMLX_E_STATE, "tp_quantized_matmul_all_sum: peers not connected");
+  if (!y || !x || !w || !scales || !biases) return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: null pointer");
+  if (bits != 4 && bits != 8) return set_error(VMLX_E_UNSUPPORTED, "bits=%d not supported (4, 8)", bits);
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return set_error(VMLX_E_UNSUPPORTED, "group_size=%d not supported", group_size);
+  if (N <= 0 || K <= 0 || K % group_size || !aligned(x, 16) || !aligned(w, 16))
+    return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: bad shape or alignment");
+  QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
+            M, N, K, 0, 1, 1, nullptr, nullptr, 0.f, (const bf16*)residual};
+  for (int r = 0; r < TP_MAX_WORLD; r++) a.tp_buf[r] = r < h->world ? h->peer_base[r] : nullptr;
+  a.tp_rank = h->rank;
+  a.tp_world = h->world;
+  a.tp_slot_bytes = h->max_bytes;
+  a.tp_slots_off = tp_fused_slots_off(h->max_bytes, h->world);
+  a.tp_flags_off = tp_fused_flags_off(h->max_bytes, h->world);
+  a.tp_epoch_off = tp_fused_epoch_off(h->max_bytes, h->world);
+  a.tp_timeout_ns = h->timeout_ns;
+  a.tp_status = h->status;
+  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, (int)M, as_stream(stream));
 }
 
 extern "C" int vmlx_tp_status(void* tp, int* code) {

@@ -25,7 +25,7 @@ from typing import List, Optional
 
 import torch
 
-from . import _lib
+from . import _lib, fast
 from ._lib import VMLXError, check
 from .llama import QuantLinear, shard_k, shard_rows
 from .ops import _stream
@@ -91,6 +91,21 @@ class Group:
         check(_lib.lib().vmlx_tp_all_sum(self._h, out.data_ptr(), x.data_ptr(), x.numel(), _stream(x)))
         return out
 
+    def quantized_matmul_all_sum(self, x: torch.Tensor, ql: "QuantLinear", residual: Optional[torch.Tensor] = None,
+                                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Row-parallel linear fused with its all-reduce (and residual add), decode sizes:
+        out = residual + all_sum(x @ dequantized(ql)^T), one kernel per rank."""
+        x = x.contiguous()
+        K = x.shape[-1]
+        M = x.numel() // K
+        N = ql.wq.shape[0]
+        if out is None:
+            out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+        check(_lib.lib().vmlx_tp_quantized_matmul_all_sum(
+            self._h, out.data_ptr(), x.data_ptr(), ql.wq.data_ptr(), ql.scales.data_ptr(), ql.biases.data_ptr(),
+            ql.group_size, ql.bits, M, N, K, residual.data_ptr() if residual is not None else None, _stream(x)))
+        return out
+
     def status(self) -> int:
         """VMLX_OK, or VMLX_E_PEER_TIMEOUT if a peer wait ran out since the last call (synchronous)."""
         if self._h is None:
@@ -135,7 +150,19 @@ class QuantizedShardedToAllLinear:
                                  ql.group_size, ql.bits)
         self.group, self.bias = group, bias
 
-    def __call__(self, x_local, out=None):
-        y = self.local(x_local, out=out)
+    def __call__(self, x_local, out=None, residual=None, fused: bool = True):
+        """allSum(x_local @ W_local^T) [+ bias] [+ residual].  Decode sizes (<= 32 rows, no
+        bias) run as one fused GEMV + all-reduce kernel per rank."""
+        rows = x_local.numel() // x_local.shape[-1]
+        if fused and self.bias is None and 1 <= rows <= 32:
+            return self.group.quantized_matmul_all_sum(x_local, self.local, residual=residual, out=out)
+        y = self.local(x_local)
         self.group.all_sum(y)
-        return y + self.bias if self.bias is not None else y
+        if self.bias is not None:
+            y = y + self.bias
+        if residual is not None:
+            y = fast.add(residual, y, out=out)
+        elif out is not None:
+            out.copy_(y)
+            y = out
+        return y

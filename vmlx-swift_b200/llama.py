@@ -118,11 +118,17 @@ class LlamaDecoder:
     """Decoder stack with per-layer bf16 KV caches [B, Hkv/P, max_len, D]."""
 
     def __init__(self, cfg: LlamaConfig, batch: int, max_len: int, dev, seed: int = 0,
-                 rank: int = 0, world: int = 1, all_sum=None, cache_fill: int = 0, fused: bool = True):
+                 rank: int = 0, world: int = 1, all_sum=None, cache_fill: int = 0, fused: bool = True,
+                 group=None):
         if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn % world:
             raise ValueError("heads / ffn not divisible by the TP size")
         self.cfg, self.B, self.max_len, self.dev = cfg, batch, max_len, dev
         self.rank, self.world, self.all_sum = rank, world, all_sum
+        # group (distributed.Group): with fused=True under TP, o_proj / down_proj run as one
+        # GEMV + all-reduce + residual kernel per rank (vmlx_tp_quantized_matmul_all_sum)
+        self.group = group
+        if all_sum is None and group is not None:
+            self.all_sum = group.all_sum
         # fused: RMSNorm folded into the q/k/v and gate/up GEMVs (x staged normalised), and at TP=1
         # the residual adds folded into the o_proj / down_proj GEMVs (in place on x)
         self.fused = fused and batch <= 32
@@ -165,6 +171,7 @@ class LlamaDecoder:
         """One decode step for B tokens at cache position `pos` (in place on x)."""
         cfg = self.cfg
         fused, tp = self.fused, self.world > 1
+        tp_fused = fused and tp and self.group is not None
         for i, L in enumerate(self.layers):
             if fused:
                 L.qkv.fused(x, norm_weight=L.norm1, eps=cfg.eps, out=self.qkv_buf)
@@ -177,6 +184,8 @@ class LlamaDecoder:
                              out=self.attn)
             if fused and not tp:
                 L.o.fused(self.attn.view(self.B, -1), residual=x, out=x)
+            elif tp_fused:
+                self.group.quantized_matmul_all_sum(self.attn.view(self.B, -1), L.o, residual=x, out=x)
             else:
                 L.o(self.attn.view(self.B, -1), out=self.proj)
                 self._reduce(self.proj)
@@ -189,6 +198,8 @@ class LlamaDecoder:
             fast.silu_mul(self.gu, out=self.act)
             if fused and not tp:
                 L.down.fused(self.act, residual=x, out=x)
+            elif tp_fused:
+                self.group.quantized_matmul_all_sum(self.act, L.down, residual=x, out=x)
             else:
                 L.down(self.act, out=self.proj)
                 self._reduce(self.proj)
@@ -198,9 +209,10 @@ class LlamaDecoder:
     # ---- CUDA-graph decode (the public per-token call) ----
     @property
     def launches_per_step(self):
-        # per layer: 4 GEMV, rope, sdpa (2 kernels), silu_mul; unfused: + 2 rms_norm; TP: + 2 all-reduce + 2 add
+        # per layer: 4 GEMV, rope, sdpa (2 kernels), silu_mul; unfused: + 2 rms_norm; TP: + 2 all-reduce
+        # + 2 add unless the row-parallel GEMVs carry the all-reduce and residual themselves
         n = 8 + (0 if self.fused else 2)
-        if self.world > 1:
+        if self.world > 1 and not (self.fused and self.group is not None):
             n += 4
         elif not self.fused:
             n += 2
