@@ -255,14 +255,15 @@ def decode_step_bytes(dec, pos):
     return dec.weight_bytes + kv_read
 
 
-def bench_decode(args, torch, vm, dev, rank, world, all_sum=None):
+def bench_decode(args, torch, vm, dev, rank, world, grp=None):
     hbm, tf, tf_s, peak_src = peaks()
     cfg = vm.llama.LlamaConfig(n_layers=args.layers)
     B, ctx = args.batch, args.ctx
     pos = ctx  # the step appends token ctx+1 after `ctx` random cached tokens
     vm.lib().vmlx_set_launch_overlap(1)
+    # TP: o_proj / down_proj run as fused GEMV + P2P all-reduce + residual kernels (group=grp)
     dec = vm.llama.LlamaDecoder(cfg, B, max_len=ctx + 8, dev=dev, seed=0, rank=rank, world=world,
-                                all_sum=all_sum, cache_fill=ctx)
+                                group=grp, cache_fill=ctx)
     stream = torch.cuda.Stream(dev)
     x0 = torch.randn(B, cfg.hidden, device=dev, generator=torch.Generator(device=dev).manual_seed(3)).bfloat16()
     x = x0.clone()
@@ -297,6 +298,27 @@ def bench_decode(args, torch, vm, dev, rank, world, all_sum=None):
     gemv_bytes_avg = (dec.weight_bytes + len(gemv_calls) * B * 2 * (cfg.hidden + dec.ffn)) / len(gemv_calls)
     gemv_achieved = gemv_bytes_avg / t_gemv / 1e9
 
+    # TP: the fused row-parallel kernels (GEMV + all-reduce + residual) alone, in lockstep on every rank
+    tp_fused = None
+    if grp is not None:
+        racc = torch.zeros(B, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        tp_calls = []
+        for L in dec.layers:
+            tp_calls += [lambda L=L: grp.quantized_matmul_all_sum(dec.attn.view(B, -1), L.o, residual=racc, out=racc),
+                         lambda L=L: grp.quantized_matmul_all_sum(dec.act, L.down, residual=racc, out=racc)]
+        t_tp = time_graph_calls(torch, tp_calls, 5, 3, stream)
+        t = torch.tensor([t_tp], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_tp = t.item()
+        w_tp = sum(L.o.nbytes + L.down.nbytes for L in dec.layers) / len(tp_calls)
+        link = (world - 1) * B * cfg.hidden * 2  # bf16 partial rows sent to the other ranks per call
+        t_target = max(w_tp / (hbm * 1e9), link / 770e9)
+        tp_fused = {"kernel": "qmv_kernel with the row-parallel all-reduce (vmlx_tp_quantized_matmul_all_sum)",
+                    "us_per_call": round(t_tp * 1e6, 2), "weight_bytes_per_call": int(w_tp),
+                    "nvlink_bytes_out_per_call": link,
+                    "roofline_us": round(t_target * 1e6, 2), "frac_of_combined_roofline": round(t_target / t_tp, 4),
+                    "roofline_basis": "max(weight bytes / measured HBM, NVLink bytes / 770 GB/s measured peer copy)"}
+
     # end to end through the public API: host token state in, host state out, every step
     xh = x0.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -328,6 +350,7 @@ def bench_decode(args, torch, vm, dev, rank, world, all_sum=None):
         "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
                 "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2},
         "gpu_launches": args.steps * dec.launches_per_step,
+        **({"tp_fused": tp_fused} if tp_fused else {}),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -422,12 +445,11 @@ def main():
         if rank == 0:
             print(json.dumps(res), flush=True)
     else:
-        all_sum, grp = None, None
+        grp = None
         if world > 1:
             # one rank per GPU: P2P all-reduce group bootstrapped over torch.distributed (NCCL only for the bootstrap)
             grp = vm.distributed.Group(strict=True)
-            all_sum = grp.all_sum
-        res = bench_decode(args, torch, vm, dev, rank, world, all_sum)
+        res = bench_decode(args, torch, vm, dev, rank, world, grp)
         if grp is not None:
             res["tp_status"] = grp.status()
         res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",

@@ -246,23 +246,24 @@ VMLX_API int vmlx_tp_set_timeout_us(void* tp, uint64_t us);
  * 16-byte aligned), identical bits on every rank (fixed rank order, fp32
  * sums).  Replaces vmlx_all_sum (Libraries/CmlxDistributedShim/CmlxDistributedShim.c:54-60)
  * behind Collectives.allSum (Libraries/MLXDistributedTP/Collectives.swift:27-32).
- * One kernel: P2P stores of this rank's data into every rank's buffer, flags
- * with release/acquire at system scope, bounded waits.  Every rank must make
+ * One kernel: P2P stores of this rank's data into every rank's buffer; small
+ * vectors (n*8 <= max_bytes) as 8-byte {value, epoch} words that the reader
+ * polls, larger ones with release/acquire flags at system scope; bounded waits.  Every rank must make
  * the same sequence of calls.  Size 1: a copy.  Stream ordered; graph-capturable.
  */
 VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, void* stream);
 
 /*
  * Row-parallel quantized linear fused with its all-reduce and the residual add
- * (decode, 1 <= M <= 32, M*N*2 <= max_bytes):
+ * (decode, 1 <= M <= 32, M*N*8 <= max_bytes):
  *   y[M, N] = bf16(residual + bf16(sum_r x_r[M, K] @ dequantize(w_r[N, K])^T))
  * where rank r holds the K-shard x_r / w_r (scales / biases [N, K/group_size]).
  * Replaces QuantizedShardedToAllLinear.callAsFunction -> Collectives.allSum
  * (Libraries/MLXDistributedTP/LinearLayers.swift:198-205, Collectives.swift:27-32)
  * plus the decoder residual add (Libraries/MLXLLM/Models/Llama.swift:110-114).
  * One kernel per rank: the GEMV pushes its bf16 partial rows into every rank's
- * slot over NVLink P2P; each CTA then waits (bounded) for the same CTA of every
- * rank and sums its rows in rank order -- bitwise equal to quantized_matmul,
+ * slot over NVLink P2P as 8-byte {value, epoch} words; each CTA then polls
+ * (bounded) the words of the rows it computed and sums them in rank order -- bitwise equal to quantized_matmul,
  * vmlx_tp_all_sum and add run separately.  residual may be NULL or alias y.
  * Every rank must make the same sequence of calls.  Size 1: the local fused GEMV.
  */

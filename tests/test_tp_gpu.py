@@ -205,4 +205,5 @@ def test_tp2_all_sum_and_decoder():
     for p in procs:
         p.join(timeout=60)
     for rank, ok, rel in res:
-        assert isinstance(ok, list) and all(ok), (rank, ok, rel)
+        assert isinstance(ok, list) and all(ok), (rank, [i for i, v in enumerate(ok) if not v] if isinstance(ok, list)
+                                                  else ok, rel)

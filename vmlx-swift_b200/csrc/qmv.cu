@@ -159,13 +159,15 @@ __device__ __forceinline__ uint2 norm4(uint2 v, float inv, const bf16* w) {
 }
 
 // Store one output element, with the optional fused residual add.  Under row-parallel
-// TP the bf16 partial goes to slot [tpp][tp_rank] of every rank instead (P2P stores).
-__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v, int tpp) {
-  if (p.tp_world > 1) {
-    const bf16 hv = __float2bfloat16_rn(v);
-    const size_t off = p.tp_slots_off + ((size_t)tpp * p.tp_world + p.tp_rank) * p.tp_slot_bytes +
-                       (size_t)((yr - p.y) + col) * sizeof(bf16);
-    for (int r = 0; r < p.tp_world; r++) *reinterpret_cast<bf16*>(p.tp_buf[r] + off) = hv;
+// TP the bf16 partial goes to slot [parity][tp_rank] of every rank instead, as one
+// low-latency word {bf16 bits, epoch} per element (P2P 8-byte stores).
+template <bool TP>
+__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v, uint32_t tp_e) {
+  if constexpr (TP) {
+    const uint32_t hv = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+    const size_t off = p.tp_slots_off + ((size_t)(tp_e & 1) * p.tp_world + p.tp_rank) * p.tp_slot_bytes +
+                       (size_t)((yr - p.y) + col) * sizeof(uint64_t);
+    for (int r = 0; r < p.tp_world; r++) st_ll(reinterpret_cast<uint64_t*>(p.tp_buf[r] + off), hv, tp_e);
     return;
   }
   if (p.residual) {
@@ -237,7 +239,7 @@ __device__ __forceinline__ uint32_t swz128(int r, int o) {
   return (uint32_t)(r * 128 + ((((o >> 4) ^ (r & 7))) << 4) + (o & 15));
 }
 
-template <int BITS, int GS, int NT, bool CC>
+template <int BITS, int GS, int NT, bool CC, bool TP>
 __global__ void __launch_bounds__(QMV_THREADS, 1)
 qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
            const __grid_constant__ CUtensorMap tmb, int sc_tma, int mode, int Ks, int C, int TOKA,
@@ -354,16 +356,11 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // Row-parallel TP: this call's epoch (advanced by the grid's last CTA) picks the slot parity.
     __shared__ uint32_t s_tp_e;
-    __shared__ int s_tp_ok;
-    if (p.tp_world > 1) {
-      if (tid == 0) {
-        s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off) + 1;
-        s_tp_ok = 1;
-      }
+    if constexpr (TP) {
+      if (tid == 0) s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off) + 1;
       named_bar_sync(1, 32 * QMV_CWARPS);
     }
-    const uint32_t tp_e = p.tp_world > 1 ? s_tp_e : 0u;
-    const int tpp = (int)(tp_e & 1);
+    const uint32_t tp_e = TP ? s_tp_e : 0u;
     for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);
       if (I.ntok == 0) continue;
@@ -595,7 +592,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 const bf16* xr_unused;
                 bf16* yr;
                 token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-                store_y(p, yr, row, acc[t][j], tpp);
+                store_y<TP>(p, yr, row, acc[t][j], tp_e);
               }
             }
           }
@@ -704,7 +701,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                     const bf16* xr_unused;
                     bf16* yr;
                     token_rows(p, mode, I.base, chunk + t, xr_unused, yr);
-                    store_y(p, yr, I.n0 + r, res[j][t], tpp);
+                    store_y<TP>(p, yr, I.n0 + r, res[j][t], tp_e);
                   }
                 } else {
                   rb[r * TOKA + t] = res[j][t];
@@ -725,7 +722,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
               const bf16* xr_unused;
               bf16* yr;
               token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-              store_y(p, yr, I.n0 + r, s, tpp);
+              store_y<TP>(p, yr, I.n0 + r, s, tp_e);
             }
           }
           red_count++;
@@ -736,40 +733,33 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
         if (lane == 0) mbar_arrive(&scempty[slot_sc]);
       }
     }
-    if (p.tp_world > 1) {
-      // ---- row-parallel all-reduce: publish, wait for the same CTA of every rank, reduce ----
-      auto flag = [&](int on_rank, int src) {
-        return reinterpret_cast<uint32_t*>(p.tp_buf[on_rank] + p.tp_flags_off) +
-               ((size_t)tpp * p.tp_world + src) * TP_FUSED_MAXC + blockIdx.x;
-      };
-      named_bar_sync(1, 32 * QMV_CWARPS);  // every partial store of this CTA is issued
-      if (tid < p.tp_world) {
-        __threadfence_system();
-        st_release_sys(flag(tid, p.tp_rank), tp_e);
-        if (!wait_flag_sys(flag(p.tp_rank, tid), tp_e, p.tp_timeout_ns)) {
-          s_tp_ok = 0;
-          if (p.tp_status) atomicExch(p.tp_status, VMLX_E_PEER_TIMEOUT);
-        }
-      }
-      named_bar_sync(1, 32 * QMV_CWARPS);
-      if (s_tp_ok) {
-        const int rlo = C > 1 ? crow_lo : 0, rhi = C > 1 ? crow_hi : QMV_ROWS, nr = rhi - rlo;
-        for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
-          const QmvItem I = qmv_item(p, mode, item, rowtiles);
-          for (int64_t i = tid; i < (int64_t)nr * I.ntok; i += 32 * QMV_CWARPS) {
-            const int64_t row = I.n0 + rlo + i % nr, tok = i / nr;
-            if (row >= p.N) continue;
-            const int64_t idx = tok * p.N + row;
-            float sum = 0.f;  // rank order: identical on every rank
-            for (int r = 0; r < p.tp_world; r++)
-              sum += __bfloat162float(*reinterpret_cast<const bf16*>(
-                  p.tp_buf[p.tp_rank] + p.tp_slots_off + ((size_t)tpp * p.tp_world + r) * p.tp_slot_bytes +
-                  (size_t)idx * sizeof(bf16)));
-            const bf16 sb = __float2bfloat16_rn(sum);
-            p.y[idx] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + __bfloat162float(sb)) : sb;
+    if constexpr (TP) {
+      // ---- row-parallel all-reduce: the rows this CTA computed, from every rank, in rank order ----
+      // (each word is polled until it carries this call's epoch: no separate flags or fences)
+      const uint64_t deadline = globaltimer() + p.tp_timeout_ns;
+      const int rlo = C > 1 ? crow_lo : 0, rhi = C > 1 ? crow_hi : QMV_ROWS, nr = rhi - rlo;
+      const uint64_t* slots = reinterpret_cast<const uint64_t*>(p.tp_buf[p.tp_rank] + p.tp_slots_off +
+                                                                (size_t)(tp_e & 1) * p.tp_world * p.tp_slot_bytes);
+      const size_t rstride = p.tp_slot_bytes / sizeof(uint64_t);
+      bool tp_ok = true;
+      for (int64_t item = cluster_id; item < n_items && tp_ok; item += n_clusters) {
+        const QmvItem I = qmv_item(p, mode, item, rowtiles);
+        for (int64_t i = tid; i < (int64_t)nr * I.ntok && tp_ok; i += 32 * QMV_CWARPS) {
+          const int64_t row = I.n0 + rlo + i % nr, tok = i / nr;
+          if (row >= p.N) continue;
+          const int64_t idx = tok * p.N + row;
+          float sum = 0.f;  // rank order: identical on every rank
+          for (int r = 0; r < p.tp_world && tp_ok; r++) {
+            uint32_t v;
+            tp_ok = wait_ll(slots + r * rstride + idx, tp_e, deadline, v);
+            sum += __bfloat162float(__ushort_as_bfloat16((unsigned short)v));
           }
+          if (!tp_ok) break;
+          const bf16 sb = __float2bfloat16_rn(sum);
+          p.y[idx] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + __bfloat162float(sb)) : sb;
         }
       }
+      if (!tp_ok && p.tp_status) atomicExch(p.tp_status, VMLX_E_PEER_TIMEOUT);
       named_bar_sync(1, 32 * QMV_CWARPS);
       if (tid == 0) {  // the grid's last CTA advances the epoch for the next call
         uint32_t* ep = reinterpret_cast<uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off);
@@ -800,9 +790,9 @@ int sm_count() {
   return n;
 }
 
-template <int BITS, int GS, int NT, bool CC>
-static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
-  auto kern = qmv_kernel<BITS, GS, NT, CC>;
+template <int BITS, int GS, int NT, bool CC, bool TP>
+static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
+  auto kern = qmv_kernel<BITS, GS, NT, CC, TP>;
   QmvPlan L;
   L.init(BITS, GS, ks, toka, CC);
   static bool attr_set = false;  // per template instance
@@ -856,6 +846,16 @@ static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   cfg.numAttrs = launch_overlap() ? 2 : 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, a, tmw, tms, tmb, sc_tma, mode, ks, C, toka, rowtiles, n_items),
                     "qmv_kernel launch");
+}
+
+// Row-parallel TP (dense mode) is its own instantiation so that the plain GEMV keeps its registers.
+template <int BITS, int GS, int NT, bool CC>
+static int launch_qmv_t(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
+  if (a.tp_world > 1) {
+    if (mode != QMV_DENSE) return set_error(VMLX_E_UNSUPPORTED, "tp: row-parallel fusion is dense-only");
+    return launch_qmv_k<BITS, GS, NT, CC, true>(a, mode, zcount, ks, C, toka, st);
+  }
+  return launch_qmv_k<BITS, GS, NT, CC, false>(a, mode, zcount, ks, C, toka, st);
 }
 
 // K-slice width for a cluster of C CTAs: whole stages of groups where the

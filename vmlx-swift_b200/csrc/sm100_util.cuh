@@ -72,6 +72,27 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Low-latency words: {payload (low 32 bits), epoch (high 32 bits)} written with one
+// 8-byte system-scope store (single-copy atomic), so a reader that sees the epoch
+// also sees the payload -- no fence or separate flag round trip.
+__device__ __forceinline__ void st_ll(uint64_t* p, uint32_t payload, uint32_t epoch) {
+  const uint64_t v = ((uint64_t)epoch << 32) | payload;
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Poll a low-latency word until it carries epoch e; false once the deadline passes.
+__device__ __forceinline__ bool wait_ll(const uint64_t* p, uint32_t e, uint64_t deadline_ns, uint32_t& payload) {
+  for (uint32_t it = 0;; it++) {
+    const uint64_t v = ld_ll(p);
+    if ((uint32_t)(v >> 32) == e) { payload = (uint32_t)v; return true; }
+    if ((it & 255) == 255 && globaltimer() > deadline_ns) return false;
+  }
+}
+
 // Wait until *f - e >= 0 (wrapping 32-bit epochs); false once deadline_ns has passed.
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t e, uint64_t timeout_ns) {
   const uint64_t deadline = globaltimer() + timeout_ns;

@@ -17,8 +17,8 @@
 //    the world's flags in its own buffer (ld.acquire.sys, bounded by a
 //    globaltimer deadline), then sums the world slots in fixed rank order
 //    (identical result on every rank) and writes the output.
-//  * The epoch of chunk c lives in device memory and is advanced by the kernel,
-//    so a captured CUDA graph can be replayed; flags are monotonic, no resets.
+//  * The call's epoch lives in device memory and is advanced by the kernel's
+//    last CTA, so a captured CUDA graph can be replayed; flags are monotonic.
 //    Two parities of slots let a rank run one call ahead of a slow peer
 //    without overwriting data that peer still reads.
 //  * A wait that runs out records VMLX_E_PEER_TIMEOUT in the handle's status
@@ -77,6 +77,19 @@ inline size_t tp_fused_epoch_off(size_t max_bytes, int world) {
 }
 inline size_t tp_total_bytes(size_t max_bytes, int world) { return tp_fused_epoch_off(max_bytes, world) + 256; }
 
+// Every all_sum call (either protocol) has one epoch for all its CTAs: read from
+// epoch[0] at the start, written back by the grid's last CTA (epoch[1] counts finished
+// CTAs).  Slot parity = epoch & 1 alternates call by call, and a low-latency word's
+// epoch is unique to its call whatever CTA wrote it.
+__device__ __forceinline__ void tp_advance_epoch(uint32_t* epoch_p, uint32_t e) {
+  __threadfence();
+  if (atomicAdd(epoch_p + 1, 1u) == gridDim.x - 1) {
+    epoch_p[1] = 0;
+    epoch_p[0] = e;
+    __threadfence();
+  }
+}
+
 // One-shot all-reduce of n bf16 elements (n * 2 <= max_bytes, chunked over CTAs).
 __global__ void __launch_bounds__(TP_THREADS)
 tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
@@ -85,11 +98,11 @@ tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf
   const int64_t e0 = (int64_t)c * chunk;
   const int64_t e1 = e0 + chunk < n ? e0 + chunk : n;
   char* mine = peers.buf[rank];
-  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(mine + tp_epoch_off(max_bytes, world)) + c;
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(mine + tp_epoch_off(max_bytes, world));
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
-    s_epoch = *epoch_p + 1;
+    s_epoch = epoch_p[0] + 1;
     s_ok = 1;
   }
   __syncthreads();
@@ -135,7 +148,46 @@ tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) *epoch_p = e;
+  if (threadIdx.x == 0) tp_advance_epoch(epoch_p, e);
+}
+
+// Low-latency all-reduce for small vectors (n * 8 <= max_bytes): every element travels as
+// one 8-byte word {bf16 bits, epoch} (single system-scope store), and readers poll the
+// words themselves, so there is no fence and no flag round trip.  Same slots, parities
+// and per-CTA epochs as the flag protocol above; same rank-order fp32 sum.
+__global__ void __launch_bounds__(TP_THREADS)
+tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
+                     bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns) {
+  const int c = blockIdx.x;
+  const int64_t e0 = (int64_t)c * chunk;
+  const int64_t e1 = e0 + chunk < n ? e0 + chunk : n;
+  char* mine = peers.buf[rank];
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(mine + tp_epoch_off(max_bytes, world));
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = epoch_p[0] + 1;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int parity = e & 1;
+  for (int r = 0; r < world; r++) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(peers.buf[r] + tp_slot_off(parity, rank, max_bytes, world));
+    for (int64_t i = e0 + threadIdx.x; i < e1; i += TP_THREADS)
+      st_ll(dst + i, (uint32_t)__bfloat16_as_ushort(in[i]), e);
+  }
+  const uint64_t deadline = globaltimer() + timeout_ns;
+  bool ok = true;
+  for (int64_t i = e0 + threadIdx.x; i < e1 && ok; i += TP_THREADS) {
+    float s = 0.f;
+    for (int r = 0; r < world && ok; r++) {
+      uint32_t v;
+      ok = wait_ll(reinterpret_cast<const uint64_t*>(mine + tp_slot_off(parity, r, max_bytes, world)) + i, e,
+                   deadline, v);
+      s += __bfloat162float(__ushort_as_bfloat16((unsigned short)v));
+    }
+    if (ok) out[i] = __float2bfloat16_rn(s);
+  }
+  if (!ok) atomicExch(status, VMLX_E_PEER_TIMEOUT);
+  __syncthreads();
+  if (threadIdx.x == 0) tp_advance_epoch(epoch_p, e);
 }
 
 static int tp_check(TpHandle* h) {
@@ -256,8 +308,12 @@ extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, v
   ctas = (n + chunk - 1) / chunk;
   TpPeers peers;
   for (int r = 0; r < TP_MAX_WORLD; r++) peers.buf[r] = r < h->world ? h->peer_base[r] : nullptr;
-  tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
-      peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
+  if ((size_t)n * 8 <= h->max_bytes)
+    tp_all_sum_ll_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
+        peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
+  else
+    tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
+        peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
   return check_launch("tp_all_sum_kernel");
 }
 
@@ -277,7 +333,7 @@ extern "C" int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x
   if (rc) return rc;
   if (M == 0 && N > 0 && K > 0) return VMLX_OK;
   if (M < 1 || M > 32) return set_error(VMLX_E_UNSUPPORTED, "tp_quantized_matmul_all_sum: M=%lld (1..32)", (long long)M);
-  if ((size_t)M * N * 2 > h->max_bytes)
+  if ((size_t)M * N * 8 > h->max_bytes)
     return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: %lld x %lld output exceeds the %zu-byte slots",
                      (long long)M, (long long)N, h->max_bytes);
   if (h->world == 1)
