@@ -188,17 +188,33 @@ def bench_gemv(args, torch, vm, dev):
         for (KK, NN) in [(4096, 14336), (14336, 4096)]:
             for b in (4, 8):
                 wsw = make_quantized(vm, torch, dev, NN, KK, b, 64, 8, 7)
-                for MM in (1, 8, 32):
+                for MM in (1, 8, 32, 128, 512):
                     xx = torch.randn(MM, KK, device=dev).bfloat16()
                     yy = torch.empty(MM, NN, device=dev, dtype=torch.bfloat16)
                     cl = [(lambda w_=w_, xx=xx, yy=yy, b=b: vm.quantized_mm(xx, *w_, bits=b, out=yy))
                           for w_ in wsw]
                     t = time_graph_calls(torch, cl, 8, 3, stream)
                     gbs = gemv_bytes(MM, NN, KK, b, 64) / t / 1e9
-                    sweep[f"K{KK}_N{NN}_b{b}_M{MM}"] = {"us": round(t * 1e6, 2), "GBps": round(gbs, 1),
-                                                        "frac_8TBps": round(gbs / 8000, 3)}
+                    row = {"us": round(t * 1e6, 2), "GBps": round(gbs, 1), "frac_8TBps": round(gbs / 8000, 3),
+                           "kernel": "qmv_kernel (GEMV, CUDA cores / mma.sync)" if MM <= 32 else
+                                     "qmm_tc_kernel (tcgen05, TMEM)"}
+                    if MM > 32:  # tensor-core regime: the tensor roofline
+                        tfs = 2.0 * MM * NN * KK / t / 1e12
+                        row.update({"TFLOPs": round(tfs, 1), "frac_of_bf16_peak": round(tfs / tf, 4)})
+                    sweep[f"K{KK}_N{NN}_b{b}_M{MM}"] = row
                 del wsw
     cpu = None if args.no_cpu else cpu_baseline_gemv(M, N, K, bits, gs, seconds=args.cpu_seconds)
+    if args.profile:
+        # one eager instance of each profiled kernel inside an NVTX range (ncu --nvtx-include vmlx_profile/):
+        # the config-1 GEMV and the config-2 M=512 gate/up GEMM on the tensor-core path
+        wg = make_quantized(vm, torch, dev, 14336, 4096, 4, 64, 1, 9)[0]
+        xg = torch.randn(512, 4096, device=dev).bfloat16()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("vmlx_profile")
+        vm.quantized_mm(x, *ws[0], out=y)
+        vm.quantized_mm(xg, *wg)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     return {
         "metric": "quantized GEMV HBM GB/s (4096x4096, 4-bit g64, M=1)",
         "value": round(achieved, 1), "unit": "GB/s", "higher_is_better": True,
@@ -355,6 +371,13 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         res["cpu_baseline"] = cpu_baseline_decode(B, ctx, cfg, seconds=args.cpu_seconds)
+    if args.profile:  # one eager decode step inside an NVTX range (ncu --nvtx-include vmlx_profile/)
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("vmlx_profile")
+            dec.step(x, pos)
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
     return res
 
 
@@ -411,6 +434,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="decode batch (config 3: 1, 16, 64)")
     ap.add_argument("--ctx", type=int, default=4096, help="cached tokens before the step")
     ap.add_argument("--layers", type=int, default=32, help="decoder blocks (Llama-3-8B has 32)")
+    ap.add_argument("--profile", action="store_true",
+                    help="after timing, run one eager instance of the profiled kernels in NVTX range vmlx_profile")
     args = ap.parse_args()
     rank, world, local = dist_env()
 
