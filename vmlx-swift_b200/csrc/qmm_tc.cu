@@ -243,6 +243,12 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
         umma_commit(&x_empty[sx]);
       }
       umma_commit(acc_full);
+      // Drain: nobody else waits for the last stages' empty-barrier arrivals, which land
+      // when their MMAs complete; wait for them here so that no arrival can reach this
+      // shared memory after the CTA exits (a later CTA on this SM may place its own
+      // barriers there).
+      for (int i = nkb - SX < 0 ? 0 : nkb - SX; i < nkb; i++) ok &= mbar_wait(&x_empty[i % SX], (i / SX) & 1);
+      for (int i = nkb - SA < 0 ? 0 : nkb - SA; i < nkb; i++) ok &= mbar_wait(&a_empty[i % SA], (i / SA) & 1);
     }
   } else if (warp >= 4) {
     // ---------------- dequantize W into the TMEM A stages ----------------

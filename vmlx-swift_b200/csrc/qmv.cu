@@ -43,6 +43,9 @@ constexpr int QMV_ROWS = 16 * QMV_CWARPS;     // rows per work item
 constexpr int QMV_THREADS = 32 * (QMV_CWARPS + 1);
 constexpr int QMV_STAGES = 6;
 constexpr int QMV_MAX_CLUSTER = 8;
+#ifndef QMV_CC_MAX_TOKENS
+#define QMV_CC_MAX_TOKENS 4  // token rows up to which 4-bit GEMVs use the CUDA-core consumer
+#endif
 
 
 template <int BITS, int GS>
@@ -871,9 +874,9 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
   constexpr int SG = QT<BITS, GS>::SG;
   const int64_t KG = a.K / GS;
   const int64_t items = ((a.N + QMV_ROWS - 1) / QMV_ROWS) * zcount;
-  // 4-bit with <= 4 token rows: the CUDA-core consumer (fewer instructions per
-  // weight than an m16n8 MMA that would be 7/8 empty)
-  const bool cc = BITS == 4 && toka <= 4;
+  // 4-bit with <= QMV_CC_MAX_TOKENS token rows: the CUDA-core consumer (fewer
+  // instructions per weight than an m16n8 MMA that would be mostly empty)
+  const bool cc = BITS == 4 && toka <= QMV_CC_MAX_TOKENS;
   auto smem_of = [&](int ks_, int toka_) {
     QmvPlan L;
     L.init(BITS, GS, ks_, toka_, cc);
