@@ -260,6 +260,119 @@ def cpu_baseline_gemv(M, N, K, bits, gs, seconds=10.0):
 
 
 # ---------------------------------------------------------------------------
+# MoE workload: Qwen3-30B-A3B-shaped SwitchGLU layer
+# ---------------------------------------------------------------------------
+
+MOE_H, MOE_E, MOE_F, MOE_K = 2048, 128, 768, 8
+MOE_EXPERT_BYTES = 3 * MOE_F * MOE_H // 2 + 3 * (MOE_F * MOE_H // 64) * 4  # gate+up+down, 4-bit g64
+
+
+def bench_moe(args, torch, vm, dev):
+    """One MoE layer for T tokens: router softmax -> top-8 (precomputed, synthetic logits ~N(0,1)),
+    SwitchGLU over the routed experts (gather_qmm gate||up, SwiGLU, gather_qmm down), and the
+    score-weighted combine.  Bytes = distinct experts routed x their packed weights (the
+    reference's per-expert weight stream) + activations."""
+    hbm, tf, tf_s, peak_src = peaks()
+    T = args.tokens
+    stream = torch.cuda.Stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    copies = 4  # rotated layers (> L2: 4 x 340 MB of experts)
+
+    def experts(n, k):
+        w = (torch.randn(MOE_E, n, k, device=dev, generator=g) * 0.02).bfloat16()
+        return vm.switch_layers.QuantizedSwitchLinear.from_weight(w)
+    layers = []
+    for _ in range(copies):
+        gate, up, down = experts(MOE_F, MOE_H), experts(MOE_F, MOE_H), experts(MOE_H, MOE_F)
+        layer = vm.switch_layers.SwitchGLU(gate, up, down)
+        layer.ensure_fused_gate_up()
+        layers.append(layer)
+    logits = torch.randn(T, MOE_E, device=dev, generator=g)
+    probs = torch.softmax(logits.float(), -1)
+    scores, inds = torch.topk(probs, MOE_K, dim=-1)
+    inds = inds.to(torch.int32)
+    scores = scores.bfloat16()
+    x = torch.randn(T, MOE_H, device=dev, generator=g).bfloat16()
+    distinct = int(torch.unique(inds).numel())
+
+    def layer_fn(L, xin):
+        y = L(xin, inds)                                   # [T, k, H]
+        return (y.float() * scores.float().unsqueeze(-1)).sum(1).bfloat16()
+    outs = [None] * copies
+    calls = [(lambda i=i: outs.__setitem__(i, layer_fn(layers[i], x))) for i in range(copies)]
+    with ClockSampler(dev.index or 0) as clk:
+        t_layer = time_graph_calls(torch, calls, max(2, args.steps // copies), max(3, args.warmup), stream)
+    nbytes = distinct * MOE_EXPERT_BYTES + T * MOE_H * 2 * 2 + T * MOE_K * MOE_F * 2 * 3
+    achieved = nbytes / t_layer / 1e9
+
+    # end to end: pinned host tokens in, layer, host out
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(T, MOE_H, dtype=torch.bfloat16).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n_e2e = max(16, args.steps // 2)
+    with torch.cuda.stream(stream):
+        xd = torch.empty_like(x)
+        for i in range(3):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(layer_fn(layers[i % copies], xd), non_blocking=True)
+        stream.synchronize()
+        e0.record(stream)
+        for i in range(n_e2e):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(layer_fn(layers[i % copies], xd), non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = e0.elapsed_time(e1) / 1e3 / n_e2e
+    cpu = None if args.no_cpu else cpu_baseline_moe(T, seconds=args.cpu_seconds)
+    return {
+        "metric": f"MoE SwitchGLU layer tokens/s (Qwen3-30B-A3B-shaped, top-8 of 128 experts, 4-bit g64, T={T})",
+        "value": round(T / t_layer, 2), "unit": "tokens/s", "higher_is_better": True,
+        "ms_per_step": t_layer * 1e3, "dtype": "bf16",
+        "config": {"workload": f"BASELINE config 4: SwitchGLU gather_qmm, hidden {MOE_H}, {MOE_E} experts, expert FFN "
+                               f"{MOE_F}, top-{MOE_K} routing from softmax of random logits, T={T} tokens, TP=1",
+                   "tokens": T, "distinct_experts": distinct, "layers_rotated": copies,
+                   "l2": f"{copies} rotated layers of {MOE_E * MOE_EXPERT_BYTES / 1e6:.0f} MB of experts (> L2)",
+                   "graph": "layer calls captured in a CUDA graph"},
+        "roofline": {"bound": "hbm", "kernel": "qmv_kernel gather modes (SwitchGLU gate||up and down)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": peak_src, "algorithmic_bytes_per_layer": nbytes, "traffic": None},
+        "e2e": {"value": round(T / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
+                "h2d_bytes_per_step": T * MOE_H * 2, "d2h_bytes_per_step": T * MOE_H * 2},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+
+
+def cpu_baseline_moe(T, seconds=10.0):
+    """The oracle's SwitchGLU (numpy per routed expert over the C dequantization) on a sample."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    rng = np.random.default_rng(0)
+
+    def qw(n, k):
+        wq, s, b = [], [], []
+        for _ in range(MOE_E):
+            a, c, d = oracle.quantize(oracle.f32_to_bf16(rng.normal(0, 0.02, (n, k)).astype(np.float32)), 64, 4)
+            wq.append(a); s.append(c); b.append(d)
+        return np.stack(wq), np.stack(s), np.stack(b)
+    gate, up, down = qw(MOE_F, MOE_H), qw(MOE_F, MOE_H), qw(MOE_H, MOE_F)
+    x = oracle.f32_to_bf16(rng.normal(size=(T, MOE_H)).astype(np.float32))
+    idx = np.argsort(-rng.normal(size=(T, MOE_E)), -1)[:, :MOE_K]
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n == 0:
+        oracle.switch_glu(x, gate, up, down, idx, 64, 4)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(T / dt, 3), "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{n} SwitchGLU layers of {T} tokens (oracle: C dequantization + numpy matmuls per routed expert)",
+            "ms_per_layer": round(dt * 1e3, 1)}
+
+
+# ---------------------------------------------------------------------------
 # decode workload (BASELINE config 3)
 # ---------------------------------------------------------------------------
 
@@ -427,13 +540,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=os.environ.get("VMLX_BENCH_WORKLOAD", "decode"),
-                    choices=["gemv", "decode"])
+                    choices=["gemv", "decode", "moe"])
     ap.add_argument("--quick", action="store_true", help="skip the config-2 sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=1, help="decode batch (config 3: 1, 16, 64)")
     ap.add_argument("--ctx", type=int, default=4096, help="cached tokens before the step")
     ap.add_argument("--layers", type=int, default=32, help="decoder blocks (Llama-3-8B has 32)")
+    ap.add_argument("--tokens", type=int, default=32, help="MoE workload: tokens per layer (config 4: 1, 32, 256)")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run one eager instance of the profiled kernels in NVTX range vmlx_profile")
     args = ap.parse_args()
@@ -451,6 +565,13 @@ def main():
     vm = load_package()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.workload == "moe":
+        res = bench_moe(args, torch, vm, dev)
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "weak",
+                    "vs_baseline": None, "data": "synthetic (seeded random experts, router logits and tokens)"})
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     if args.workload == "gemv":
         if world > 1:
             # the single-matrix GEMV does not shard: N independent replicas

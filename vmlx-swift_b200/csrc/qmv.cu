@@ -304,11 +304,18 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
 
   bool ok = true;
   uint32_t it_stage = 0, ic = 0;
+  // Item order: round-robin over clusters for dense calls (x is staged once per CTA); a
+  // contiguous block per cluster in the gather modes, so that consecutive items share an
+  // expert's (or batch element's) token rows and x is staged once per token set, not per item.
+  const bool blocked = mode != QMV_DENSE;
+  const int64_t it_lo = blocked ? cluster_id * n_items / n_clusters : cluster_id;
+  const int64_t it_hi = blocked ? (cluster_id + 1) * n_items / n_clusters : n_items;
+  const int64_t it_step = blocked ? 1 : n_clusters;
 
   if (warp == QMV_CWARPS) {
     // ======================= producer warp (lane 0 issues) =======================
     bool pend = false;
-    for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
+    for (int64_t item = it_lo; item < it_hi; item += it_step) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);
       if (I.ntok == 0) continue;
       const int ybase = (int)(I.e * p.N + I.n0);  // row coordinate in the [E*N, .] maps
@@ -364,7 +371,8 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
       named_bar_sync(1, 32 * QMV_CWARPS);
     }
     const uint32_t tp_e = TP ? s_tp_e : 0u;
-    for (int64_t item = cluster_id; item < n_items; item += n_clusters) {
+    int64_t staged_z = -1;  // token set (item / rowtiles) whose x is staged
+    for (int64_t item = it_lo; item < it_hi; item += it_step) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);
       if (I.ntok == 0) continue;
       int slot_sc = 0;
@@ -396,7 +404,9 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
 
       for (int64_t chunk = 0; chunk < I.ntok; chunk += TOKA) {
         const int ntok = (int)((I.ntok - chunk) < TOKA ? (I.ntok - chunk) : TOKA);
-        if (mode != QMV_DENSE || !x_staged || I.ntok > TOKA) {
+        const int64_t z = item / rowtiles;
+        if (!x_staged || I.ntok > TOKA || (mode != QMV_DENSE && z != staged_z)) {
+          staged_z = z;
           // stage x of this chunk in fragment order, with per-group sums
           named_bar_sync(1, 32 * QMV_CWARPS);  // nobody still reads the previous chunk
           if (p.norm_w) {
