@@ -121,6 +121,18 @@ VMLX_API int vmlx_cuda_quantized_matmul_fused(void* y, const void* x, const uint
                                               void* stream);
 
 /*
+ * Down projection with the MLP's SwiGLU fused into the GEMV (decode, M <= 32):
+ *   y = [residual +] bf16(x @ dequantize(W)^T),  x = bf16(bf16(silu(gate)) * up)
+ * with gate_up bf16 [M, 2K] = gate | up; the SwiGLU is computed while x is staged,
+ * exactly as vmlx_cuda_silu_mul rounds it (compiledSwiGLU,
+ * Libraries/MLXLMCommon/SwitchLayers.swift:40-50, then the down QuantizedLinear of
+ * Libraries/MLXLLM/Models/Llama.swift:96-99).  residual may be NULL or alias y.
+ */
+VMLX_API int vmlx_cuda_quantized_matmul_swiglu(void* y, const void* gate_up, const uint32_t* w, const void* scales,
+                                               const void* biases, int group_size, int bits, int64_t M, int64_t N,
+                                               int64_t K, const void* residual, void* stream);
+
+/*
  * Gathered quantized matmul over a stack of E expert matrices.
  * Replaces mlx_gather_qmm (Source/Cmlx/include/mlx/c/ops.h:475-488), the op
  * behind QuantizedSwitchLinear.callAsFunction
@@ -179,8 +191,13 @@ VMLX_API size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int6
  *   out[b, h, :] = softmax(scale * q[b, h] . K[b, h/G, :kv_len]^T) V[b, h/G, :kv_len]
  * q bf16 [batch, n_heads, 128]; caches as for vmlx_cuda_rope_qkv; G =
  * n_heads / n_kv_heads in 1..8 (grouped-query attention).  fp32 softmax and
- * accumulation.  The cache is split over CTAs; `workspace` (caller-owned,
- * vmlx_cuda_sdpa_decode_workspace bytes) holds the per-split partials.
+ * accumulation.  The cache is split over CTAs of 128 positions; one kernel
+ * computes the splits and the last split of each (sequence, kv head) combines
+ * them.  `workspace` (caller-owned, vmlx_cuda_sdpa_decode_workspace bytes for
+ * the largest kv_len used) holds split counters followed by the per-split
+ * partials: it must be zero-filled once before its first use, every call
+ * leaves the counters zero again, and a workspace serves one (batch, n_heads)
+ * at a time.
  * Replaces MLXFast.scaledDotProductAttention for decode
  * (Source/MLX/MLXFast.swift:118; kernels mlx-generated/metal/sdpa_vector.h:15-394).
  */
@@ -195,9 +212,9 @@ VMLX_API int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache
  * by the engine, a host that forbids allocation on its inference thread, or
  * code that must not risk a cudaMalloc mid-decode).  The per-split partials
  * live in an 8 MiB array inside the library's device image (held on every GPU
- * that loads the library until the process exits); calls needing more
- * (batch * n_heads * min(128, ceil(kv_len/128)) * (head_dim + 2) * 4 bytes) are
- * rejected with VMLX_E_INVALID.  The first call on a device looks up the
+ * that loads the library until the process exits), after 64 KiB of split
+ * counters; calls needing more (batch * n_heads * ceil(kv_len/128) *
+ * (head_dim + 2) * 4 bytes of partials) are rejected with VMLX_E_INVALID.  The first call on a device looks up the
  * array's address with that device current, so make it before any stream
  * capture.  All calls on a device share the array: calls that may overlap on
  * the GPU race.  Nothing needs clearing between calls.  No counterpart in the
@@ -270,6 +287,16 @@ VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, voi
 VMLX_API int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x, const uint32_t* w,
                                               const void* scales, const void* biases, int group_size, int bits,
                                               int64_t M, int64_t N, int64_t K, const void* residual, void* stream);
+
+/*
+ * As vmlx_tp_quantized_matmul_all_sum with the MLP's SwiGLU fused into the
+ * GEMV's staging of x: gate_up bf16 [M, 2K] = gate | up (this rank's shard), the
+ * GEMV input is bf16(bf16(silu(gate)) * up) as vmlx_cuda_silu_mul computes it.
+ */
+VMLX_API int vmlx_tp_quantized_matmul_swiglu_all_sum(void* tp, void* y, const void* gate_up, const uint32_t* w,
+                                                     const void* scales, const void* biases, int group_size,
+                                                     int bits, int64_t M, int64_t N, int64_t K, const void* residual,
+                                                     void* stream);
 
 /*
  * Reads (synchronously) and clears the group's device status word:

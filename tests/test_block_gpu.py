@@ -163,3 +163,22 @@ def test_fused_gemv_matches_separate_kernels(vm, orc, cuda, M):
         y = res.clone()
         vm.ops.quantized_mm_fused(x, wq, s, b, bits=bits, norm_weight=nw, residual=y, out=y)  # in place
         assert torch.equal(y, got)
+
+
+@pytest.mark.parametrize("M", [1, 4, 9])
+def test_swiglu_fused_down_gemv_matches_separate_kernels(vm, orc, cuda, M):
+    """The SwiGLU computed while the down GEMV stages x rounds exactly as silu_mul: the fused
+    call equals silu_mul -> quantized_mm (-> add) bit for bit (4-bit CUDA-core and MMA paths, 8-bit)."""
+    K, N = 1536, 512
+    g = torch.Generator(cuda).manual_seed(10 + M)
+    for bits in (4, 8):
+        w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+        wq, s, b = vm.quantized(w, bits=bits)
+        gu = (torch.randn(M, 2 * K, device=cuda, generator=g) * 2).bfloat16()
+        res = torch.randn(M, N, device=cuda, generator=g).bfloat16()
+        act = vm.fast.silu_mul(gu)
+        assert torch.equal(vm.ops.quantized_mm_swiglu(gu, wq, s, b, bits=bits), vm.quantized_mm(act, wq, s, b, bits=bits))
+        ref = vm.ops.quantized_mm_fused(act, wq, s, b, bits=bits, residual=res)
+        y = res.clone()
+        vm.ops.quantized_mm_swiglu(gu, wq, s, b, bits=bits, residual=y, out=y)
+        assert torch.equal(y, ref)

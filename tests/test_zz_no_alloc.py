@@ -35,7 +35,7 @@ def _with_workspace(vm, q, kc, vc, kv_len):
     lib = vm.lib()
     B, Hq, D = q.shape
     nbytes = lib.vmlx_cuda_sdpa_decode_workspace(B, Hq, kv_len, D)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=q.device)  # split counters start at zero
     out = torch.empty_like(q)
     st = torch.cuda.current_stream().cuda_stream
     rc = lib.vmlx_cuda_sdpa_decode(out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), B, Hq, kc.shape[1],

@@ -68,6 +68,9 @@ SIGNATURES = {
     "vmlx_tp_all_sum": (_int, [_vp, _vp, _vp, _i64, _vp]),
     "vmlx_tp_quantized_matmul_all_sum": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64,
                                                 _vp, _vp]),
+    "vmlx_tp_quantized_matmul_swiglu_all_sum": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64,
+                                                       _i64, _vp, _vp]),
+    "vmlx_cuda_quantized_matmul_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64, _vp, _vp]),
     "vmlx_tp_status": (_int, [_vp, _c.POINTER(_int)]),
     "vmlx_tp_destroy": (_int, [_vp]),
 }

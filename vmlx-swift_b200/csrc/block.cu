@@ -12,6 +12,7 @@
 // with bulk copies (TMA engine) into shared memory and splits the cache over
 // CTAs, writing fp32 partials (m, l, o) that a second kernel combines.
 #include "kernels.cuh"
+#include "tmap.cuh"
 #include "sm100_util.cuh"
 
 #include <mutex>
@@ -106,36 +107,49 @@ __global__ void rope_qkv_kernel(const bf16* __restrict__ qkv, bf16* __restrict__
 }
 
 // ------------------------------------------------------------ decode SDPA --
-// One CTA per (cache split, kv head, batch); warp w serves q head kvh*G + w.
-// The CTA streams its [chunk x D] slices of K and V with bulk copies into a
-// double-buffered shared-memory ring.  Lane (p = lane/4, part = lane%4) owns
-// dims [32*part, 32*part+32) of positions p, p+8, ...: a score is four lanes'
-// partial dots joined by two shuffles, and each lane keeps an online softmax
-// (m, l) and 32 output dims, merged across the 8 position lanes at the end.
-// Partials (m, l, o[D]) of each (batch, q head, split) go to `part`; the
-// combine kernel rescales and sums them (flash-decoding).
+// One CTA per (cache split of up to 128 positions, kv head, sequence), 8 warps:
+// the G q heads of the kv head get 8/G warps each, which split the positions of
+// every 32-position stage.  K and V slices arrive as 2-D TMA boxes [32 positions
+// x 64 dims] with the 128-byte swizzle into a 4-stage ring (the whole split is in
+// flight at once); the swizzle keeps the eight positions a warp reads at once on
+// different banks.  Lane (p = lane/4, part = lane%4) owns dims
+// [32*part, 32*part+32) of positions p, p+8*wph, ...:
+// a score is four lanes' partial dots joined by two shuffles, each lane keeps an
+// online softmax (m, l) and 32 output dims, merged across position lanes, then
+// across the head's warps through shared memory.  The split's partial
+// (m, l, o[D]) goes to the workspace; the last CTA of each (sequence, kv head)
+// to finish -- a counter in the workspace, reset by that CTA -- combines the
+// splits (flash-decoding) and writes the output, so one launch does both.
 constexpr int SDPA_D = 128;
-constexpr int SDPA_SUB = 32;  // positions per shared-memory stage
+constexpr int SDPA_SUB = 32;     // positions per shared-memory stage
+constexpr int SDPA_STAGES = 4;   // ring depth: 4 x (K + V) x 32 positions = 64 KB
+constexpr int SDPA_CHUNK = SDPA_SUB * SDPA_STAGES;  // positions per split
+constexpr int SDPA_THREADS = 256;
+constexpr size_t SDPA_RING = (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16);
+constexpr size_t SDPA_SMEM = SDPA_RING + 64 + 1024;  // + alignment slack
 
-constexpr int SDPA_STAGES = 4;  // ring depth: 4 x (K + V) x 32 positions = 64 KB
-constexpr size_t SDPA_SMEM = (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16) + 64;
-
-__global__ void __launch_bounds__(256)
-sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
-                   float* __restrict__ part, int Hq, int Hkv, int kv_len, int max_len, int chunk, float scale_log2) {
-  extern __shared__ __align__(128) uint8_t sdpa_smem[];
-  bf16* ring = reinterpret_cast<bf16*>(sdpa_smem);  // [stage][K|V][SUB][D]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sdpa_smem + (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16));
+__global__ void __launch_bounds__(SDPA_THREADS)
+sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tmk,
+                   const __grid_constant__ CUtensorMap tmv, float* __restrict__ part, unsigned* __restrict__ counters, bf16* __restrict__ out, int Hq, int Hkv,
+                   int kv_len, int max_len, float scale_log2) {
+  extern __shared__ __align__(1024) uint8_t sdpa_smem_raw[];
+  uint8_t* sdpa_smem = sdpa_smem_raw + ((1024 - (smem_u32(sdpa_smem_raw) & 1023)) & 1023);
+  bf16* ring = reinterpret_cast<bf16*>(sdpa_smem);  // [stage][K|V][2 boxes][SUB][64], 128-byte swizzle
+  uint64_t* full = reinterpret_cast<uint64_t*>(sdpa_smem + SDPA_RING);
+  float* mrg = reinterpret_cast<float*>(sdpa_smem);  // [warp][D + 2], reuses the ring after the loop
+  __shared__ int s_last;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int n_splits = gridDim.x;
   const int G = Hq / Hkv;
+  const int wph = (SDPA_THREADS / 32) % G == 0 ? (SDPA_THREADS / 32) / G : 1;  // warps per q head
+  const int nw = G * wph;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = lane >> 2, pt = lane & 3;
-  const int hq = kvh * G + warp;
-  const int t0 = split * chunk;
-  const int t1 = min(kv_len, t0 + chunk);
-  const int n_splits = gridDim.x;
-  const bf16* kbase = kc + ((int64_t)b * Hkv + kvh) * max_len * SDPA_D;
-  const bf16* vbase = vc + ((int64_t)b * Hkv + kvh) * max_len * SDPA_D;
+  const int g = warp % G, sub = warp / G;
+  const int hq = kvh * G + g;
+  const int t0 = split * SDPA_CHUNK;
+  const int t1 = min(kv_len, t0 + SDPA_CHUNK);
+  const int row0 = ((int)b * Hkv + kvh) * max_len;  // this head's first cache row in the [rows, D] maps
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SDPA_STAGES; s++) mbar_init(&full[s], 1);
@@ -145,22 +159,31 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
   // the cache and q may come from the previous kernel (launch overlap): wait for it
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  const int nsub = t1 > t0 ? (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB : 0;
-  auto kst = [&](int s) { return ring + ((size_t)(s % SDPA_STAGES) * 2 + 0) * SDPA_SUB * SDPA_D; };
-  auto vst = [&](int s) { return ring + ((size_t)(s % SDPA_STAGES) * 2 + 1) * SDPA_SUB * SDPA_D; };
-  auto issue = [&](int s) {
-    const int a = t0 + s * SDPA_SUB;
-    const int n = min(SDPA_SUB, t1 - a);
-    const uint32_t bytes = (uint32_t)n * SDPA_D * 2;
-    mbar_arrive_expect_tx(&full[s % SDPA_STAGES], 2 * bytes);
-    bulk_g2s(kst(s), kbase + (int64_t)a * SDPA_D, bytes, &full[s % SDPA_STAGES]);
-    bulk_g2s(vst(s), vbase + (int64_t)a * SDPA_D, bytes, &full[s % SDPA_STAGES]);
+  const int nsub = t1 > t0 ? (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB : 0;  // <= SDPA_STAGES
+  auto kst = [&](int s) { return ring + ((size_t)s * 2 + 0) * SDPA_SUB * SDPA_D; };
+  auto vst = [&](int s) { return ring + ((size_t)s * 2 + 1) * SDPA_SUB * SDPA_D; };
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+    for (int s = 0; s < nsub; s++) {
+      // two [32 x 64] boxes per matrix (dims 0-63, 64-127); rows past the cache read as zeros
+      const int row = row0 + t0 + s * SDPA_SUB;
+      mbar_arrive_expect_tx(&full[s], 4 * SDPA_SUB * 128);
+      tma_load_2d(kst(s), &tmk, 0, row, &full[s]);
+      tma_load_2d(kst(s) + SDPA_SUB * 64, &tmk, 64, row, &full[s]);
+      tma_load_2d(vst(s), &tmv, 0, row, &full[s]);
+      tma_load_2d(vst(s) + SDPA_SUB * 64, &tmv, 64, row, &full[s]);
+    }
+  }
+  // lane's 16-byte chunk i of position pp: box pt/2, chunk (pt%2)*4 + i, swizzled by pp & 7
+  auto swz = [&](const bf16* st, int pp, int i) {
+    return reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(st) + (pt >> 1) * (SDPA_SUB * 128) +
+                                          pp * 128 + ((((pt & 1) * 4 + i) ^ (pp & 7)) << 4));
   };
-  if (threadIdx.x == 0)
-    for (int s = 0; s < nsub && s < SDPA_STAGES; s++) issue(s);
 
+  const bool active = warp < nw;
   float qf[32];
-  if (warp < G) {
+  if (active) {
     const bf16* qr = q + ((int64_t)b * Hq + hq) * SDPA_D + pt * 32;
 #pragma unroll
     for (int i = 0; i < 32; i += 8) {
@@ -178,21 +201,19 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
 #pragma unroll
   for (int i = 0; i < 32; i++) o[i] = 0.f;
 
-  bool ok = true;
   for (int s = 0; s < nsub; s++) {
-    ok &= mbar_wait(&full[s % SDPA_STAGES], (s / SDPA_STAGES) & 1);
+    mbar_wait(&full[s], 0);
     const int n = min(SDPA_SUB, t1 - (t0 + s * SDPA_SUB));
-    if (warp < G) {
+    if (active) {
       const bf16* ks = kst(s);
       const bf16* vs = vst(s);
-      for (int pp = p; pp < SDPA_SUB; pp += 8) {
+      for (int pp = p + 8 * sub; pp < SDPA_SUB; pp += 8 * wph) {
         const bool valid = pp < n;
         float d = 0.f;
         if (valid) {
-          const bf16* kr = ks + pp * SDPA_D + pt * 32;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 v = *reinterpret_cast<const uint4*>(kr + i);
+            uint4 v = *swz(ks, pp, i >> 3);
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -209,10 +230,9 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
           const float corr = exp2f(m - mn);
           const float pw = exp2f(d - mn);
           l = l * corr + pw;
-          const bf16* vr = vs + pp * SDPA_D + pt * 32;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 v = *reinterpret_cast<const uint4*>(vr + i);
+            uint4 v = *swz(vs, pp, i >> 3);
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -225,10 +245,10 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
         }
       }
     }
-    __syncthreads();  // stage s is free: refill it with sub s + STAGES
-    if (threadIdx.x == 0 && s + SDPA_STAGES < nsub) issue(s + SDPA_STAGES);
   }
-  if (warp < G) {
+  // the next kernel may start streaming its own inputs while this grid finishes
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (active) {
     // merge the 8 position lanes that share `pt`
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
@@ -245,34 +265,80 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc, cons
       l = l * c1 + l2 * c2;
       m = mn;
     }
-    float* dst = part + (((int64_t)b * Hq + hq) * n_splits + split) * (SDPA_D + 2);
-    if (p == 0) {
+  }
+  __syncthreads();  // every stage consumed: the ring becomes the merge buffer
+  if (active && p == 0) {
+    float* w = mrg + warp * (SDPA_D + 2);
 #pragma unroll
-      for (int i = 0; i < 32; i++) dst[2 + pt * 32 + i] = o[i];
-      if (pt == 0) {
-        dst[0] = m;
-        dst[1] = l;
-      }
+    for (int i = 0; i < 32; i++) w[2 + pt * 32 + i] = o[i];
+    if (pt == 0) {
+      w[0] = m;
+      w[1] = l;
     }
   }
-  (void)ok;
-}
-
-// out[b, hq, :] = sum_s exp2(m_s - M) o_s / sum_s exp2(m_s - M) l_s
-__global__ void sdpa_combine_kernel(const float* __restrict__ part, bf16* __restrict__ out, int n_splits) {
-  const int64_t bh = blockIdx.x;
-  const float* src = part + bh * n_splits * (SDPA_D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < n_splits; s++) M = fmaxf(M, src[s * (SDPA_D + 2)]);
-  const int d = threadIdx.x;
-  float acc = 0.f, L = 0.f;
-  for (int s = 0; s < n_splits; s++) {
-    const float ms = src[s * (SDPA_D + 2)];
-    const float c = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-    L += c * src[s * (SDPA_D + 2) + 1];
-    acc += c * src[s * (SDPA_D + 2) + 2 + d];
+  __syncthreads();
+  // merge the head's warps, write this split's partial (m, l, o[D])
+  for (int t = threadIdx.x; t < G * SDPA_D; t += SDPA_THREADS) {
+    const int gg = t / SDPA_D, dd = t % SDPA_D;
+    float mm = -INFINITY;
+    for (int s2 = 0; s2 < wph; s2++) mm = fmaxf(mm, mrg[(s2 * G + gg) * (SDPA_D + 2)]);
+    float ll = 0.f, oo = 0.f;
+    for (int s2 = 0; s2 < wph; s2++) {
+      const float* w = mrg + (s2 * G + gg) * (SDPA_D + 2);
+      const float c = (w[0] == -INFINITY) ? 0.f : exp2f(w[0] - mm);
+      ll += c * w[1];
+      oo += c * w[2 + dd];
+    }
+    float* dst = part + (((int64_t)b * Hq + kvh * G + gg) * n_splits + split) * (SDPA_D + 2);
+    dst[2 + dd] = oo;
+    if (dd == 0) {
+      dst[0] = mm;
+      dst[1] = ll;
+    }
   }
-  out[bh * SDPA_D + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  // last split of this (sequence, kv head) to finish combines: out = sum c_s o_s / sum c_s l_s
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* cnt = counters + (int64_t)b * Hkv + kvh;
+    s_last = atomicAdd(cnt, 1u) == (unsigned)(n_splits - 1);
+    if (s_last) *cnt = 0u;  // ready for the next call
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // per (head, split): weight c = exp2(m - M_head) and sum c*l, computed in parallel through
+  // shared memory (the ring is free), then each output dim sums c*o over the splits
+  float* cw = mrg;                 // [G][n_splits] weights
+  float* lsum = mrg + G * n_splits;  // [G]
+  const int64_t bh0 = (int64_t)b * Hq + kvh * G;
+  const float* src0 = part + bh0 * n_splits * (SDPA_D + 2);
+  for (int t = threadIdx.x; t < G * n_splits; t += SDPA_THREADS) cw[t] = __ldcg(src0 + (int64_t)t * (SDPA_D + 2));
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int gg = threadIdx.x;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_splits; s2++) M = fmaxf(M, cw[gg * n_splits + s2]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < n_splits; s2++) {
+      const float ms = cw[gg * n_splits + s2];
+      const float c = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+      cw[gg * n_splits + s2] = c;
+      L += c * __ldcg(src0 + ((int64_t)gg * n_splits + s2) * (SDPA_D + 2) + 1);
+    }
+    lsum[gg] = L;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < G * SDPA_D; t += SDPA_THREADS) {
+    const int gg = t / SDPA_D, dd = t % SDPA_D;
+    const float* src = src0 + (int64_t)gg * n_splits * (SDPA_D + 2) + 2 + dd;
+    const float* c = cw + gg * n_splits;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < n_splits; s2++) acc = fmaf(c[s2], __ldcg(src + (int64_t)s2 * (SDPA_D + 2)), acc);
+    const float L = lsum[gg];
+    out[(bh0 + gg) * SDPA_D + dd] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  }
 }
 
 // ----------------------------------------------------------- SwiGLU / add --
@@ -335,11 +401,24 @@ extern "C" int vmlx_cuda_rope_qkv(void* q_out, void* k_cache, void* v_cache, con
 }
 
 static int sdpa_splits(int64_t kv_len) {
-  int64_t s = (kv_len + 127) / 128;  // ~128 cache positions per CTA
-  return (int)(s < 1 ? 1 : (s > 128 ? 128 : s));
+  const int64_t s = (kv_len + SDPA_CHUNK - 1) / SDPA_CHUNK;  // SDPA_CHUNK cache positions per CTA
+  return (int)(s < 1 ? 1 : s);
 }
 
-static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, float* part, bf16* out, int64_t batch,
+// Workspace: one split counter per (sequence, head) first -- at a fixed place, so that calls
+// with a growing kv_len find them zero -- then the per-split partials.
+static size_t sdpa_cnt_bytes(int64_t batch, int n_heads) {
+  return ((size_t)batch * n_heads * sizeof(unsigned) + 255) / 256 * 256;
+}
+static size_t sdpa_part_bytes(int64_t batch, int n_heads, int64_t kv_len) {
+  return (size_t)batch * n_heads * sdpa_splits(kv_len) * (SDPA_D + 2) * sizeof(float);
+}
+static size_t sdpa_ws_bytes(int64_t batch, int n_heads, int64_t kv_len) {
+  return sdpa_cnt_bytes(batch, n_heads) + sdpa_part_bytes(batch, n_heads, kv_len);
+}
+
+static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
+                       int64_t batch,
                        int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
@@ -349,11 +428,20 @@ static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, float* par
     attr = true;
   }
   const int splits = sdpa_splits(kv_len);
-  const int chunk = (int)((kv_len + splits - 1) / splits);
-  const int G = n_heads / n_kv_heads;
+  // the combining CTA keeps a weight per (head, split) in the 64 KB ring
+  if (splits > 65535 || (size_t)(splits + 1) * (n_heads / n_kv_heads) * sizeof(float) > SDPA_RING)
+    return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: kv_len=%lld too long", (long long)kv_len);
+  const int64_t rows = batch * n_kv_heads * max_len;
+  if (rows >= (1LL << 31)) return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: cache of %lld rows", (long long)rows);
+  CUtensorMap tmk, tmv;
+  if (!make_tmap_2d(&tmk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kc, SDPA_D, (uint64_t)rows, SDPA_D * 2, 64, SDPA_SUB,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tmv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vc, SDPA_D, (uint64_t)rows, SDPA_D * 2, 64, SDPA_SUB,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return VMLX_E_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
-  cfg.blockDim = dim3(32 * G);
+  cfg.blockDim = dim3(SDPA_THREADS);
   cfg.dynamicSmemBytes = SDPA_SMEM;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -361,16 +449,14 @@ static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, float* par
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = launch_overlap() ? 1 : 0;
-  int rc = check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel, q, kc, vc, part, n_heads, n_kv_heads, (int)kv_len,
-                                         (int)max_len, chunk, scale * 1.4426950408889634f),
-                      "sdpa_decode_kernel launch");
-  if (rc) return rc;
-  sdpa_combine_kernel<<<(unsigned)(batch * n_heads), SDPA_D, 0, st>>>(part, out, splits);
-  return check_launch("sdpa_combine_kernel");
+  return check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel, q, tmk, tmv, part, counters, out, n_heads, n_kv_heads,
+                                       (int)kv_len, (int)max_len, scale * 1.4426950408889634f),
+                    "sdpa_decode_kernel launch");
 }
 
 extern "C" size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int64_t kv_len, int head_dim) {
-  return (size_t)batch * n_heads * sdpa_splits(kv_len) * (head_dim + 2) * sizeof(float);
+  (void)head_dim;
+  return sdpa_ws_bytes(batch, n_heads, kv_len);
 }
 
 extern "C" int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache, const void* v_cache,
@@ -389,8 +475,9 @@ extern "C" int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cac
   if (workspace_bytes < need)
     return set_error(VMLX_E_INVALID, "sdpa_decode: workspace of %zu bytes, %zu needed", workspace_bytes, need);
   if (batch == 0) return VMLX_OK;
-  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, (float*)workspace, (bf16*)out,
-                     batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
+  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, static_cast<unsigned*>(workspace),
+                     reinterpret_cast<float*>(static_cast<char*>(workspace) + sdpa_cnt_bytes(batch, n_heads)),
+                     (bf16*)out, batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
 }
 
 extern "C" int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, int64_t ffn, void* stream) {
@@ -423,18 +510,21 @@ extern "C" int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n,
 //
 // Limits and behaviour:
 //  * the array holds SDPA_NOALLOC_BYTES (8 MiB) per GPU, for as long as the
-//    process has the library loaded on that GPU; calls whose partials need
-//    more (batch * n_heads * ceil(kv_len/128, at most 128) * (head_dim + 2) * 4
-//    bytes) are rejected with VMLX_E_INVALID;
+//    process has the library loaded on that GPU: 64 KiB of split counters
+//    (zero when the library loads; every call leaves them zero) and the
+//    partials; calls whose partials need more (batch * n_heads *
+//    ceil(kv_len/128) * (head_dim + 2) * 4 bytes) than the rest are rejected
+//    with VMLX_E_INVALID;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
 //    before any stream capture;
 //  * every call on a device shares the one array: calls that can overlap on
 //    the GPU (different streams without ordering) race and must not be issued;
-//  * each call writes every partial it later reads, so nothing needs clearing
-//    and stale contents of an earlier call are never used.
+//  * each call writes every partial it later reads, so stale partials of an
+//    earlier call are never used.
 // ---------------------------------------------------------------------------
 constexpr size_t SDPA_NOALLOC_BYTES = (size_t)8 << 20;
+constexpr size_t SDPA_NOALLOC_CNT_BYTES = (size_t)64 << 10;  // split counters (zero at load; calls leave them zero)
 static __device__ __align__(256) float g_sdpa_noalloc_scratch[SDPA_NOALLOC_BYTES / sizeof(float)];
 
 static std::mutex g_noalloc_mu;
@@ -470,16 +560,17 @@ extern "C" int vmlx_cuda_sdpa_decode_noalloc(void* out, const void* q, const voi
     return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: kv_len=%lld", (long long)kv_len);
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16))
     return set_error(VMLX_E_INVALID, "sdpa_decode_noalloc: pointers must be 16-byte aligned");
-  const size_t need = vmlx_cuda_sdpa_decode_workspace(batch, n_heads, kv_len, head_dim);
-  if (need > SDPA_NOALLOC_BYTES)
+  const size_t need = sdpa_part_bytes(batch, n_heads, kv_len);
+  if (need > SDPA_NOALLOC_BYTES - SDPA_NOALLOC_CNT_BYTES || (size_t)batch * n_heads * 4 > SDPA_NOALLOC_CNT_BYTES)
     return set_error(VMLX_E_INVALID,
                      "sdpa_decode_noalloc: these sizes need %zu bytes of partials, more than the %zu-byte "
                      "built-in scratch; use vmlx_cuda_sdpa_decode with a workspace",
-                     need, SDPA_NOALLOC_BYTES);
+                     need, SDPA_NOALLOC_BYTES - SDPA_NOALLOC_CNT_BYTES);
   if (batch == 0) return VMLX_OK;
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, (float*)scratch, (bf16*)out,
+  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, static_cast<unsigned*>(scratch),
+                     reinterpret_cast<float*>(static_cast<char*>(scratch) + SDPA_NOALLOC_CNT_BYTES), (bf16*)out,
                      batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
 }

@@ -28,6 +28,10 @@ struct QmvArgs {
   const bf16* norm_w;   // x <- norm_w * bf16(x * rsqrt(mean(x^2) + eps)) over the full row
   float eps;
   const bf16* residual;  // y <- bf16(residual + bf16(x @ W^T)), residual laid out like y (may alias y)
+  // x_swiglu (dense): x is a [M, 2K] gate||up buffer and the GEMV input is
+  // bf16(bf16(silu(gate)) * up), computed while x is staged (the SwiGLU of the MLP fused
+  // into the down projection)
+  int x_swiglu;
   // Row-parallel tensor parallelism (tp_world > 1, dense mode): the bf16 partial y of
   // this rank goes into slot [parity][tp_rank] of every rank's buffer over P2P; each
   // CTA then waits for the same CTA of every rank and reduces its rows in rank order:

@@ -87,3 +87,22 @@ extern "C" int vmlx_cuda_quantized_matmul_fused(void* y, const void* x, const ui
             M, N, K, 0, 1, 1, nullptr, (const bf16*)norm_weight, eps, (const bf16*)residual};
   return launch_qmv(a, QMV_DENSE, bits, group_size, 1, toka_for(M), as_stream(stream));
 }
+
+// Down projection with the MLP's SwiGLU fused into the GEMV's x staging (decode, M <= 32):
+//   y = [residual +] bf16(SwiGLU(gate_up) @ dequantize(W)^T),  gate_up bf16 [M, 2K] = gate | up
+// -- compiledSwiGLU followed by the down QuantizedLinear (Libraries/MLXLMCommon/SwitchLayers.swift:40-50,
+// Libraries/MLXLLM/Models/Llama.swift:96-99) in one kernel.
+extern "C" int vmlx_cuda_quantized_matmul_swiglu(void* y, const void* gate_up, const uint32_t* w, const void* scales,
+                                                 const void* biases, int group_size, int bits, int64_t M, int64_t N,
+                                                 int64_t K, const void* residual, void* stream) {
+  if (M == 0 && N > 0 && K > 0) return VMLX_OK;
+  int rc = check_mm_args(y, gate_up, w, scales, biases, true, group_size, bits, "affine", M, N, K);
+  if (rc) return rc;
+  if (M > 32) return set_error(VMLX_E_UNSUPPORTED, "quantized_matmul_swiglu: M=%lld > 32", (long long)M);
+  if (K % 8) return set_error(VMLX_E_INVALID, "quantized_matmul_swiglu: K must be a multiple of 8");
+  QmvArgs a{(const bf16*)gate_up, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
+            M, N, K, 0, 1, 1, nullptr, nullptr, 0.f, (const bf16*)residual};
+  a.x_swiglu = 1;
+  return launch_qmv(a, QMV_DENSE, bits, group_size, 1, toka_for(M), as_stream(stream));
+}
+

@@ -43,6 +43,9 @@ constexpr int QMV_ROWS = 16 * QMV_CWARPS;     // rows per work item
 constexpr int QMV_THREADS = 32 * (QMV_CWARPS + 1);
 constexpr int QMV_STAGES = 6;
 constexpr int QMV_MAX_CLUSTER = 8;
+#ifndef QMV_MAX_PER_SM
+#define QMV_MAX_PER_SM 3  // cap on resident CTAs per SM assumed by the cost model
+#endif
 #ifndef QMV_CC_MAX_TOKENS
 #define QMV_CC_MAX_TOKENS 4  // token rows up to which 4-bit GEMVs use the CUDA-core consumer
 #endif
@@ -71,7 +74,7 @@ __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t* a, int64_t n,
 __device__ __forceinline__ void token_rows(const QmvArgs& p, int mode, int64_t b_or_r0, int64_t tok,
                                            const bf16*& xr, bf16*& yr) {
   if (mode == QMV_DENSE) {
-    xr = p.x + tok * p.K;
+    xr = p.x + tok * (p.x_swiglu ? 2 * p.K : p.K);
     yr = p.y + tok * p.N;
   } else if (mode == QMV_GATHER) {
     int64_t b = b_or_r0;
@@ -159,6 +162,28 @@ __device__ __forceinline__ uint2 norm4(uint2 v, float inv, const bf16* w) {
     o[j] = bf162_as_u32(__floats2bfloat162_rn(wf.x * n.x, wf.y * n.y));
   }
   return make_uint2(o[0], o[1]);
+}
+
+// SwiGLU of a gate||up row on load: bf16(bf16(silu(g)) * u), the rounding of
+// compiledSwiGLU and of the standalone silu_mul kernel.
+__device__ __forceinline__ uint32_t swiglu2(uint32_t g, uint32_t u) {
+  const float2 gf = __bfloat1622float2(u32_as_bf162(g)), uf = __bfloat1622float2(u32_as_bf162(u));
+  const float s0 = __bfloat162float(__float2bfloat16_rn(gf.x / (1.f + __expf(-gf.x))));
+  const float s1 = __bfloat162float(__float2bfloat16_rn(gf.y / (1.f + __expf(-gf.y))));
+  return bf162_as_u32(__floats2bfloat162_rn(s0 * uf.x, s1 * uf.y));
+}
+// 8 (or 4) x values at xrow[off]: plain, or the SwiGLU of gate xrow[off] and up xrow[K + off]
+__device__ __forceinline__ uint4 load_x8(const QmvArgs& p, const bf16* xrow) {
+  const uint4 v = *reinterpret_cast<const uint4*>(xrow);
+  if (!p.x_swiglu) return v;
+  const uint4 u = *reinterpret_cast<const uint4*>(xrow + p.K);
+  return make_uint4(swiglu2(v.x, u.x), swiglu2(v.y, u.y), swiglu2(v.z, u.z), swiglu2(v.w, u.w));
+}
+__device__ __forceinline__ uint2 load_x4(const QmvArgs& p, const bf16* xrow) {
+  const uint2 v = *reinterpret_cast<const uint2*>(xrow);
+  if (!p.x_swiglu) return v;
+  const uint2 u = *reinterpret_cast<const uint2*>(xrow + p.K);
+  return make_uint2(swiglu2(v.x, u.x), swiglu2(v.y, u.y));
 }
 
 // Store one output element, with the optional fused residual add.  Under row-parallel
@@ -447,7 +472,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
 #pragma unroll
               for (int q = 0; q < 4; q++) {
                 uint4 v = make_uint4(0, 0, 0, 0);
-                if (xrow) v = *reinterpret_cast<const uint4*>(xrow + q * 8);
+                if (xrow) v = load_x8(p, xrow + q * 8);
                 if (xrow && p.norm_w) v = norm8(v, xinv[tok], p.norm_w + gs0 * GS + ci * 32 + q * 8);
                 const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
                 const float2 c2 = __bfloat1622float2(u32_as_bf162(v.z)), d2 = __bfloat1622float2(u32_as_bf162(v.w));
@@ -475,7 +500,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 uint8_t* dst = xfrag + ((((size_t)gl * WPL + wi) * TOKA + tok) * 4 + cc) * FB;
                 if constexpr (BITS == 4) {
                   uint4 v = make_uint4(0, 0, 0, 0);
-                  if (xrow) v = *reinterpret_cast<const uint4*>(xrow + cc * VPL + wi * 8);
+                  if (xrow) v = load_x8(p, xrow + cc * VPL + wi * 8);
                   if (xrow && p.norm_w) v = norm8(v, xinv[tok], p.norm_w + (gs0 + gl) * GS + cc * VPL + wi * 8);
                   uint4 f;
                   f.x = prmt(v.x, v.y, 0x5410);  // (x0, x2)
@@ -488,7 +513,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                   sum += ((a.x + a.y) + (b2.x + b2.y)) + ((c2.x + c2.y) + (d2.x + d2.y));
                 } else {
                   uint2 v = make_uint2(0, 0);
-                  if (xrow) v = *reinterpret_cast<const uint2*>(xrow + cc * VPL + wi * 4);
+                  if (xrow) v = load_x4(p, xrow + cc * VPL + wi * 4);
                   if (xrow && p.norm_w) v = norm4(v, xinv[tok], p.norm_w + (gs0 + gl) * GS + cc * VPL + wi * 4);
                   *reinterpret_cast<uint2*>(dst) = v;
                   const float2 a = __bfloat1622float2(u32_as_bf162(v.x)), b2 = __bfloat1622float2(u32_as_bf162(v.y));
@@ -836,6 +861,7 @@ static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, QMV_THREADS, L.total);
   if (e != cudaSuccess || per_sm < 1) per_sm = 1;
+  if (per_sm > QMV_MAX_PER_SM) per_sm = QMV_MAX_PER_SM;
   int64_t max_clusters = (int64_t)sm_count() * per_sm / C;
   if (max_clusters < 1) max_clusters = 1;
   const int64_t n_clusters = n_items < max_clusters ? n_items : max_clusters;
@@ -903,7 +929,8 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     const size_t sm = smem_of(ks, toka);
     if (sm > 226 * 1024) continue;
     int per_sm = (int)((228 * 1024) / (sm + 1024));
-    const int reg_cap = cc ? 2 : 3;  // 160 threads x ~150 (CUDA-core) / ~128 (MMA) registers
+    int reg_cap = cc ? 2 : 3;  // 160 threads x ~150 (CUDA-core) / ~128 (MMA) registers
+    if (reg_cap > QMV_MAX_PER_SM) reg_cap = QMV_MAX_PER_SM;
     per_sm = per_sm > reg_cap ? reg_cap : (per_sm < 1 ? 1 : per_sm);
     const int64_t clusters = (int64_t)sm_count() * per_sm / C;
     if (clusters < 1) continue;

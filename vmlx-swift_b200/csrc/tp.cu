@@ -324,10 +324,28 @@ extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, v
 // the decoder's residual add (Libraries/MLXLLM/Models/Llama.swift:110-114).  Decode sizes
 // (M <= 32): the GEMV pushes its bf16 partial rows straight into every rank's slot
 // over NVLink and reduces them in the same kernel.
+static int tp_qmm_all_sum(void* tp, void* y, const void* x, const uint32_t* w, const void* scales,
+                          const void* biases, int group_size, int bits, int64_t M, int64_t N, int64_t K,
+                          const void* residual, int swiglu, void* stream);
+
 extern "C" int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x, const uint32_t* w,
                                                 const void* scales, const void* biases, int group_size, int bits,
                                                 int64_t M, int64_t N, int64_t K, const void* residual,
                                                 void* stream) {
+  return tp_qmm_all_sum(tp, y, x, w, scales, biases, group_size, bits, M, N, K, residual, 0, stream);
+}
+
+// The same with the MLP's SwiGLU fused into the staging of x: x is the [M, 2K] gate||up buffer.
+extern "C" int vmlx_tp_quantized_matmul_swiglu_all_sum(void* tp, void* y, const void* gate_up, const uint32_t* w,
+                                                       const void* scales, const void* biases, int group_size,
+                                                       int bits, int64_t M, int64_t N, int64_t K,
+                                                       const void* residual, void* stream) {
+  return tp_qmm_all_sum(tp, y, gate_up, w, scales, biases, group_size, bits, M, N, K, residual, 1, stream);
+}
+
+static int tp_qmm_all_sum(void* tp, void* y, const void* x, const uint32_t* w, const void* scales,
+                          const void* biases, int group_size, int bits, int64_t M, int64_t N, int64_t K,
+                          const void* residual, int swiglu, void* stream) {
   TpHandle* h = static_cast<TpHandle*>(tp);
   int rc = tp_check(h);
   if (rc) return rc;
@@ -337,8 +355,10 @@ extern "C" int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x
     return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: %lld x %lld output exceeds the %zu-byte slots",
                      (long long)M, (long long)N, h->max_bytes);
   if (h->world == 1)
-    return vmlx_cuda_quantized_matmul_fused(y, x, w, scales, biases, group_size, bits, M, N, K, nullptr, 0.f, residual,
-                                            stream);
+    return swiglu ? vmlx_cuda_quantized_matmul_swiglu(y, x, w, scales, biases, group_size, bits, M, N, K, residual,
+                                                      stream)
+                  : vmlx_cuda_quantized_matmul_fused(y, x, w, scales, biases, group_size, bits, M, N, K, nullptr, 0.f,
+                                                     residual, stream);
   if (!h->connected) return set_error(VMLX_E_STATE, "tp_quantized_matmul_all_sum: peers not connected");
   if (!y || !x || !w || !scales || !biases) return set_error(VMLX_E_INVALID, "tp_quantized_matmul_all_sum: null pointer");
   if (bits != 4 && bits != 8) return set_error(VMLX_E_UNSUPPORTED, "bits=%d not supported (4, 8)", bits);
@@ -357,6 +377,8 @@ extern "C" int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x
   a.tp_epoch_off = tp_fused_epoch_off(h->max_bytes, h->world);
   a.tp_timeout_ns = h->timeout_ns;
   a.tp_status = h->status;
+  a.x_swiglu = swiglu;
+  if (swiglu && K % 8) return set_error(VMLX_E_INVALID, "tp: SwiGLU input needs K a multiple of 8");
   return launch_qmv(a, QMV_DENSE, bits, group_size, 1, (int)M, as_stream(stream));
 }
 

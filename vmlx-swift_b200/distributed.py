@@ -92,16 +92,19 @@ class Group:
         return out
 
     def quantized_matmul_all_sum(self, x: torch.Tensor, ql: "QuantLinear", residual: Optional[torch.Tensor] = None,
-                                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                                 out: Optional[torch.Tensor] = None, swiglu: bool = False) -> torch.Tensor:
         """Row-parallel linear fused with its all-reduce (and residual add), decode sizes:
-        out = residual + all_sum(x @ dequantized(ql)^T), one kernel per rank."""
+        out = residual + all_sum(x @ dequantized(ql)^T), one kernel per rank.  swiglu: x is the
+        [.., 2K] gate||up shard and the GEMV input is silu(gate) * up (computed on load)."""
         x = x.contiguous()
-        K = x.shape[-1]
-        M = x.numel() // K
+        K = x.shape[-1] // (2 if swiglu else 1)
+        M = x.numel() // x.shape[-1]
         N = ql.wq.shape[0]
         if out is None:
             out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
-        check(_lib.lib().vmlx_tp_quantized_matmul_all_sum(
+        fn = (_lib.lib().vmlx_tp_quantized_matmul_swiglu_all_sum if swiglu
+              else _lib.lib().vmlx_tp_quantized_matmul_all_sum)
+        check(fn(
             self._h, out.data_ptr(), x.data_ptr(), ql.wq.data_ptr(), ql.scales.data_ptr(), ql.biases.data_ptr(),
             ql.group_size, ql.bits, M, N, K, residual.data_ptr() if residual is not None else None, _stream(x)))
         return out

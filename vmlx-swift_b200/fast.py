@@ -59,7 +59,7 @@ def sdpa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, k
     scale = D ** -0.5 if scale is None else scale
     need = sdpa_workspace_bytes(B, Hq, kv_len, D)
     if workspace is None:
-        workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=q.device)
+        workspace = torch.zeros(max(need, 4), dtype=torch.uint8, device=q.device)
     out = torch.empty_like(q) if out is None else out
     check(_lib.lib().vmlx_cuda_sdpa_decode(out.data_ptr(), q.contiguous().data_ptr(), k_cache.data_ptr(),
                                            v_cache.data_ptr(), B, Hq, Hkv, D, kv_len, k_cache.shape[2], scale,

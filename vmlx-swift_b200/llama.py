@@ -53,6 +53,11 @@ class QuantLinear:
         return ops.quantized_mm(x, self.wq, self.scales, self.biases, group_size=self.group_size,
                                 bits=self.bits, out=out)
 
+    def fused_swiglu(self, gate_up, residual=None, out=None):
+        """silu(gate) * up -> matmul -> [+ residual], one kernel (decode, M <= 32)."""
+        return ops.quantized_mm_swiglu(gate_up, self.wq, self.scales, self.biases, group_size=self.group_size,
+                                       bits=self.bits, residual=residual, out=out)
+
     def fused(self, x, norm_weight=None, eps=1e-5, residual=None, out=None):
         """x -> [RMSNorm] -> matmul -> [+ residual], one kernel (decode, M <= 32)."""
         return ops.quantized_mm_fused(x, self.wq, self.scales, self.biases, group_size=self.group_size,
@@ -156,7 +161,7 @@ class LlamaDecoder:
         self.proj = torch.empty(batch, cfg.hidden, **bf)
         self.gu = torch.empty(batch, 2 * self.ffn, **bf)
         self.act = torch.empty(batch, self.ffn, **bf)
-        self.ws = torch.empty(max(fast.sdpa_workspace_bytes(batch, self.hq, max_len, D), 4),
+        self.ws = torch.zeros(max(fast.sdpa_workspace_bytes(batch, self.hq, max_len, D), 4),
                               dtype=torch.uint8, device=dev)
 
     @property
@@ -195,12 +200,12 @@ class LlamaDecoder:
             else:
                 fast.rms_norm(x, L.norm2, cfg.eps, out=self.h)
                 L.gate_up(self.h, out=self.gu)
-            fast.silu_mul(self.gu, out=self.act)
-            if fused and not tp:
-                L.down.fused(self.act, residual=x, out=x)
+            if fused and not tp:  # SwiGLU fused into the down GEMV's x staging
+                L.down.fused_swiglu(self.gu, residual=x, out=x)
             elif tp_fused:
-                self.group.quantized_matmul_all_sum(self.act, L.down, residual=x, out=x)
+                self.group.quantized_matmul_all_sum(self.gu, L.down, residual=x, out=x, swiglu=True)
             else:
+                fast.silu_mul(self.gu, out=self.act)
                 L.down(self.act, out=self.proj)
                 self._reduce(self.proj)
                 fast.add(x, self.proj, out=x)
@@ -209,10 +214,11 @@ class LlamaDecoder:
     # ---- CUDA-graph decode (the public per-token call) ----
     @property
     def launches_per_step(self):
-        # per layer: 4 GEMV, rope, sdpa (2 kernels), silu_mul; unfused: + 2 rms_norm; TP: + 2 all-reduce
-        # + 2 add unless the row-parallel GEMVs carry the all-reduce and residual themselves
-        n = 8 + (0 if self.fused else 2)
-        if self.world > 1 and not (self.fused and self.group is not None):
+        # per layer: 4 GEMV, rope, sdpa (one kernel, combine fused); unfused: + silu_mul + 2 rms_norm;
+        # TP: + 2 all-reduce + 2 add unless the row-parallel GEMVs carry the all-reduce and residual
+        tp_fused = self.world > 1 and self.fused and self.group is not None
+        n = 6 + (0 if self.fused and (self.world == 1 or tp_fused) else 1) + (0 if self.fused else 2)
+        if self.world > 1 and not tp_fused:
             n += 4
         elif not self.fused:
             n += 2

@@ -137,6 +137,24 @@ def quantized_mm_fused(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, b
     return out
 
 
+def quantized_mm_swiglu(gate_up: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                        group_size: int = 64, bits: int = 4, residual: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Down projection with the MLP's SwiGLU fused into the GEMV (M <= 32):
+    ``[residual +] silu(gate) * up @ dequantized(w)^T`` for ``gate_up = gate | up`` [..., 2K]."""
+    _need_cuda(gate_up, w, scales, biases, residual)
+    gate_up = gate_up.contiguous()
+    K = gate_up.shape[-1] // 2
+    N = w.shape[-2]
+    M = gate_up.numel() // (2 * K) if K else 0
+    if out is None:
+        out = torch.empty(*gate_up.shape[:-1], N, dtype=torch.bfloat16, device=gate_up.device)
+    check(_lib.lib().vmlx_cuda_quantized_matmul_swiglu(
+        out.data_ptr(), gate_up.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), group_size, bits,
+        M, N, K, residual.data_ptr() if residual is not None else None, _stream(gate_up)))
+    return out
+
+
 def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                         biases: Optional[torch.Tensor], lhs_indices: Optional[torch.Tensor] = None,
                         rhs_indices: Optional[torch.Tensor] = None, transpose: bool = True,
