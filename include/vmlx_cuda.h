@@ -191,7 +191,7 @@ VMLX_API size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int6
  *   out[b, h, :] = softmax(scale * q[b, h] . K[b, h/G, :kv_len]^T) V[b, h/G, :kv_len]
  * q bf16 [batch, n_heads, 128]; caches as for vmlx_cuda_rope_qkv; G =
  * n_heads / n_kv_heads in 1..8 (grouped-query attention).  fp32 softmax and
- * accumulation.  The cache is split over CTAs of 128 positions; one kernel
+ * accumulation.  The cache is split over CTAs of 256 positions; one kernel
  * computes the splits and the last split of each (sequence, kv head) combines
  * them.  `workspace` (caller-owned, vmlx_cuda_sdpa_decode_workspace bytes for
  * the largest kv_len used) holds split counters followed by the per-split
@@ -213,7 +213,7 @@ VMLX_API int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cache
  * code that must not risk a cudaMalloc mid-decode).  The per-split partials
  * live in an 8 MiB array inside the library's device image (held on every GPU
  * that loads the library until the process exits), after 64 KiB of split
- * counters; calls needing more (batch * n_heads * ceil(kv_len/128) *
+ * counters; calls needing more (batch * n_heads * ceil(kv_len/256) *
  * (head_dim + 2) * 4 bytes of partials) are rejected with VMLX_E_INVALID.  The first call on a device looks up the
  * array's address with that device current, so make it before any stream
  * capture.  All calls on a device share the array: calls that may overlap on

@@ -107,46 +107,46 @@ __global__ void rope_qkv_kernel(const bf16* __restrict__ qkv, bf16* __restrict__
 }
 
 // ------------------------------------------------------------ decode SDPA --
-// One CTA per (cache split of up to 128 positions, kv head, sequence), 8 warps:
-// the G q heads of the kv head get 8/G warps each, which split the positions of
-// every 32-position stage.  K and V slices arrive as 2-D TMA boxes [32 positions
-// x 64 dims] with the 128-byte swizzle into a 4-stage ring (the whole split is in
-// flight at once); the swizzle keeps the eight positions a warp reads at once on
-// different banks.  Lane (p = lane/4, part = lane%4) owns dims
-// [32*part, 32*part+32) of positions p, p+8*wph, ...:
-// a score is four lanes' partial dots joined by two shuffles, each lane keeps an
-// online softmax (m, l) and 32 output dims, merged across position lanes, then
-// across the head's warps through shared memory.  The split's partial
-// (m, l, o[D]) goes to the workspace; the last CTA of each (sequence, kv head)
-// to finish -- a counter in the workspace, reset by that CTA -- combines the
-// splits (flash-decoding) and writes the output, so one launch does both.
+// One CTA per (cache split of up to 256 positions, kv head, sequence), 8 warps:
+// warp w takes the split's 32-position stage w.  K and V arrive as 2-D TMA boxes
+// [32 positions x 64 dims] with the 128-byte swizzle (the whole split is in
+// flight at once).  The math runs on the tensor cores (mma.sync m16n8k16, bf16
+// in, fp32 accumulate): the G q heads of the kv head are the rows of
+// S = Q K^T (K fragments read straight from the swizzled tiles, bank-conflict
+// free), the softmax of the stage stays in registers, and P (bf16) is the A
+// operand of O = P V (V fragments by ldmatrix.trans).  The warps' (m, l, O) are
+// merged through shared memory into the split's partial; the last CTA of each
+// (sequence, kv head) to finish -- a counter in the workspace, reset by that CTA
+// -- combines the splits (flash-decoding) and writes the output.
 constexpr int SDPA_D = 128;
-constexpr int SDPA_SUB = 32;     // positions per shared-memory stage
-constexpr int SDPA_STAGES = 4;   // ring depth: 4 x (K + V) x 32 positions = 64 KB
+constexpr int SDPA_SUB = 32;     // positions per stage (one warp each)
+constexpr int SDPA_STAGES = 8;   // stages per split: 8 x (K + V) x 32 positions = 128 KB
 constexpr int SDPA_CHUNK = SDPA_SUB * SDPA_STAGES;  // positions per split
-constexpr int SDPA_THREADS = 256;
+constexpr int SDPA_THREADS = 32 * SDPA_STAGES;
 constexpr size_t SDPA_RING = (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16);
 constexpr size_t SDPA_SMEM = SDPA_RING + 64 + 1024;  // + alignment slack
 
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 __global__ void __launch_bounds__(SDPA_THREADS)
 sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tmk,
-                   const __grid_constant__ CUtensorMap tmv, float* __restrict__ part, unsigned* __restrict__ counters, bf16* __restrict__ out, int Hq, int Hkv,
-                   int kv_len, int max_len, float scale_log2) {
+                   const __grid_constant__ CUtensorMap tmv, float* __restrict__ part, unsigned* __restrict__ counters,
+                   bf16* __restrict__ out, int Hq, int Hkv, int kv_len, int max_len, float scale_log2) {
   extern __shared__ __align__(1024) uint8_t sdpa_smem_raw[];
   uint8_t* sdpa_smem = sdpa_smem_raw + ((1024 - (smem_u32(sdpa_smem_raw) & 1023)) & 1023);
-  bf16* ring = reinterpret_cast<bf16*>(sdpa_smem);  // [stage][K|V][2 boxes][SUB][64], 128-byte swizzle
+  uint8_t* ring = sdpa_smem;  // [stage][K|V][2 boxes][32 positions][128 B], 128-byte swizzle
   uint64_t* full = reinterpret_cast<uint64_t*>(sdpa_smem + SDPA_RING);
-  float* mrg = reinterpret_cast<float*>(sdpa_smem);  // [warp][D + 2], reuses the ring after the loop
+  float* mrg = reinterpret_cast<float*>(sdpa_smem);  // [warp][head][D + 2], reuses the ring after the math
   __shared__ int s_last;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int n_splits = gridDim.x;
   const int G = Hq / Hkv;
-  const int wph = (SDPA_THREADS / 32) % G == 0 ? (SDPA_THREADS / 32) / G : 1;  // warps per q head
-  const int nw = G * wph;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int p = lane >> 2, pt = lane & 3;
-  const int g = warp % G, sub = warp / G;
-  const int hq = kvh * G + g;
+  const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates: head row g, column pair c
   const int t0 = split * SDPA_CHUNK;
   const int t1 = min(kv_len, t0 + SDPA_CHUNK);
   const int row0 = ((int)b * Hkv + kvh) * max_len;  // this head's first cache row in the [rows, D] maps
@@ -160,8 +160,8 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int nsub = t1 > t0 ? (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB : 0;  // <= SDPA_STAGES
-  auto kst = [&](int s) { return ring + ((size_t)s * 2 + 0) * SDPA_SUB * SDPA_D; };
-  auto vst = [&](int s) { return ring + ((size_t)s * 2 + 1) * SDPA_SUB * SDPA_D; };
+  auto kst = [&](int s) { return ring + ((size_t)s * 2 + 0) * SDPA_SUB * SDPA_D * 2; };
+  auto vst = [&](int s) { return ring + ((size_t)s * 2 + 1) * SDPA_SUB * SDPA_D * 2; };
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmk);
     tma_prefetch_desc(&tmv);
@@ -170,124 +170,125 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
       const int row = row0 + t0 + s * SDPA_SUB;
       mbar_arrive_expect_tx(&full[s], 4 * SDPA_SUB * 128);
       tma_load_2d(kst(s), &tmk, 0, row, &full[s]);
-      tma_load_2d(kst(s) + SDPA_SUB * 64, &tmk, 64, row, &full[s]);
+      tma_load_2d(kst(s) + SDPA_SUB * 128, &tmk, 64, row, &full[s]);
       tma_load_2d(vst(s), &tmv, 0, row, &full[s]);
-      tma_load_2d(vst(s) + SDPA_SUB * 64, &tmv, 64, row, &full[s]);
+      tma_load_2d(vst(s) + SDPA_SUB * 128, &tmv, 64, row, &full[s]);
     }
   }
-  // lane's 16-byte chunk i of position pp: box pt/2, chunk (pt%2)*4 + i, swizzled by pp & 7
-  auto swz = [&](const bf16* st, int pp, int i) {
-    return reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(st) + (pt >> 1) * (SDPA_SUB * 128) +
-                                          pp * 128 + ((((pt & 1) * 4 + i) ^ (pp & 7)) << 4));
+  // byte offset of (position r, dim d) in a swizzled [32 x 128] stage tile (two [32 x 64] boxes)
+  auto tile_off = [](int r, int d) {
+    return (uint32_t)((d >> 6) * (SDPA_SUB * 128) + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
   };
 
-  const bool active = warp < nw;
-  float qf[32];
-  if (active) {
-    const bf16* qr = q + ((int64_t)b * Hq + hq) * SDPA_D + pt * 32;
+  // Q as the A operand: rows = the G heads (rows >= G and g + 8 are zero), k = dims
+  const bool hv = g < G;
+  const bf16* qr = q + ((int64_t)b * Hq + kvh * G + (hv ? g : 0)) * SDPA_D;
+  uint32_t qa0[8], qa2[8];
 #pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-      uint4 v = *reinterpret_cast<const uint4*>(qr + i);
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
-        qf[i + 2 * j] = f.x * scale_log2;
-        qf[i + 2 * j + 1] = f.y * scale_log2;
-      }
-    }
+  for (int ks = 0; ks < 8; ks++) {
+    qa0[ks] = hv ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * c) : 0u;
+    qa2[ks] = hv ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * c + 8) : 0u;
   }
-  float m = -INFINITY, l = 0.f, o[32];
+  float m = -INFINITY, l = 0.f;
+  float o[16][4];
 #pragma unroll
-  for (int i = 0; i < 32; i++) o[i] = 0.f;
+  for (int nd = 0; nd < 16; nd++) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
 
-  for (int s = 0; s < nsub; s++) {
+  const int s = warp;
+  if (s < nsub) {
     mbar_wait(&full[s], 0);
     const int n = min(SDPA_SUB, t1 - (t0 + s * SDPA_SUB));
-    if (active) {
-      const bf16* ks = kst(s);
-      const bf16* vs = vst(s);
-      for (int pp = p + 8 * sub; pp < SDPA_SUB; pp += 8 * wph) {
-        const bool valid = pp < n;
-        float d = 0.f;
-        if (valid) {
+    const uint8_t* kt = kst(s);
+    const uint32_t vt = smem_u32(vst(s));
+    // S = Q K^T: 4 n-tiles of 8 positions x 8 k-steps of 16 dims
+    float sc[4][4];
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v = *swz(ks, pp, i >> 3);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    for (int nt = 0; nt < 4; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
-              d = fmaf(qf[i + 2 * j], f.x, d);
-              d = fmaf(qf[i + 2 * j + 1], f.y, d);
-            }
-          }
-        }
-        d += __shfl_xor_sync(0xffffffffu, d, 1);
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        if (valid) {  // online softmax in base 2 (scores carry log2(e) * scale)
-          const float mn = fmaxf(m, d);
-          const float corr = exp2f(m - mn);
-          const float pw = exp2f(d - mn);
-          l = l * corr + pw;
+    for (int ks = 0; ks < 8; ks++) {
+      const uint32_t a[4] = {qa0[ks], 0u, qa2[ks], 0u};
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v = *swz(vs, pp, i >> 3);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      for (int nt = 0; nt < 4; nt++) {
+        const int r = nt * 8 + g;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + tile_off(r, 16 * ks + 2 * c));
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kt + tile_off(r, 16 * ks + 2 * c + 8));
+        mma_bf16_16816(sc[nt], a, b0, b1);
+      }
+    }
+    // softmax of the stage in base 2: lane holds positions nt*8 + 2c (+1) of head g
+    float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              float2 f = __bfloat1622float2(u32_as_bf162(u[j]));
-              o[i + 2 * j] = fmaf(o[i + 2 * j], corr, pw * f.x);
-              o[i + 2 * j + 1] = fmaf(o[i + 2 * j + 1], corr, pw * f.y);
-            }
-          }
-          m = mn;
-        }
+    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const float v = (nt * 8 + 2 * c + j < n) ? sc[nt][j] * scale_log2 : -INFINITY;
+        sc[nt][j] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    m = mx;
+    // P = P_hi + P_lo, both bf16 (P_lo = the rounding residue), so the tensor-core P V keeps
+    // ~16 bits of each probability, as close to the reference's fp32 as the sums need
+    uint32_t pa[2][4], pl[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; nt++) {
+      const float p0 = exp2f(sc[nt][0] - m), p1 = exp2f(sc[nt][1] - m);
+      l += p0 + p1;
+      const bf162 hi = __floats2bfloat162_rn(p0, p1);
+      const float2 hf = __bfloat1622float2(hi);
+      const uint32_t pk = bf162_as_u32(hi), pr = bf162_as_u32(__floats2bfloat162_rn(p0 - hf.x, p1 - hf.y));
+      // A fragment of P for k-step nt/2: positions 16*ks2 + 2c (a0) and + 8 (a2); rows g + 8 are zero
+      if (nt & 1) { pa[nt >> 1][2] = pk; pl[nt >> 1][2] = pr; } else { pa[nt >> 1][0] = pk; pl[nt >> 1][0] = pr; }
+    }
+    pa[0][1] = pa[0][3] = pa[1][1] = pa[1][3] = 0u;
+    pl[0][1] = pl[0][3] = pl[1][1] = pl[1][3] = 0u;
+    // O = P V: 2 k-steps of 16 positions x 16 n-tiles of 8 dims; V fragments by ldmatrix.trans
+    // (lanes 0-7 / 8-15 / 16-23 / 24-31 address rows 0-7 / 8-15 of dims nd*8 and nd*8 + 8)
+#pragma unroll
+    for (int ks2 = 0; ks2 < 2; ks2++) {
+      const int r = 16 * ks2 + (lane & 15);
+#pragma unroll
+      for (int nd = 0; nd < 16; nd += 2) {
+        const int d = (nd + (lane >> 4)) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(vt + tile_off(r, d), b0, b1, b2, b3);
+        mma_bf16_16816(o[nd], pa[ks2], b0, b1);
+        mma_bf16_16816(o[nd + 1], pa[ks2], b2, b3);
+        mma_bf16_16816(o[nd], pl[ks2], b0, b1);
+        mma_bf16_16816(o[nd + 1], pl[ks2], b2, b3);
       }
     }
   }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
   // the next kernel may start streaming its own inputs while this grid finishes
   asm volatile("griddepcontrol.launch_dependents;");
-  if (active) {
-    // merge the 8 position lanes that share `pt`
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-      const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
-      const float mn = fmaxf(m, m2);
-      const float c1 = (m == -INFINITY) ? 0.f : exp2f(m - mn);
-      const float c2 = (m2 == -INFINITY) ? 0.f : exp2f(m2 - mn);
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const float o2 = __shfl_xor_sync(0xffffffffu, o[i], off);
-        o[i] = o[i] * c1 + o2 * c2;
-      }
-      l = l * c1 + l2 * c2;
-      m = mn;
-    }
-  }
   __syncthreads();  // every stage consumed: the ring becomes the merge buffer
-  if (active && p == 0) {
-    float* w = mrg + warp * (SDPA_D + 2);
+  if (hv) {
+    float* w = mrg + ((size_t)warp * G + g) * (SDPA_D + 2);
 #pragma unroll
-    for (int i = 0; i < 32; i++) w[2 + pt * 32 + i] = o[i];
-    if (pt == 0) {
+    for (int nd = 0; nd < 16; nd++) {
+      w[2 + nd * 8 + 2 * c] = o[nd][0];
+      w[2 + nd * 8 + 2 * c + 1] = o[nd][1];
+    }
+    if (c == 0) {
       w[0] = m;
       w[1] = l;
     }
   }
   __syncthreads();
-  // merge the head's warps, write this split's partial (m, l, o[D])
+  // merge the warps (stages), write this split's partial (m, l, o[D])
   for (int t = threadIdx.x; t < G * SDPA_D; t += SDPA_THREADS) {
     const int gg = t / SDPA_D, dd = t % SDPA_D;
     float mm = -INFINITY;
-    for (int s2 = 0; s2 < wph; s2++) mm = fmaxf(mm, mrg[(s2 * G + gg) * (SDPA_D + 2)]);
+    for (int s2 = 0; s2 < SDPA_STAGES; s2++) mm = fmaxf(mm, mrg[((size_t)s2 * G + gg) * (SDPA_D + 2)]);
     float ll = 0.f, oo = 0.f;
-    for (int s2 = 0; s2 < wph; s2++) {
-      const float* w = mrg + (s2 * G + gg) * (SDPA_D + 2);
-      const float c = (w[0] == -INFINITY) ? 0.f : exp2f(w[0] - mm);
-      ll += c * w[1];
-      oo += c * w[2 + dd];
+    for (int s2 = 0; s2 < SDPA_STAGES; s2++) {
+      const float* w = mrg + ((size_t)s2 * G + gg) * (SDPA_D + 2);
+      const float cw = (w[0] == -INFINITY) ? 0.f : exp2f(w[0] - mm);
+      ll += cw * w[1];
+      oo += cw * w[2 + dd];
     }
     float* dst = part + (((int64_t)b * Hq + kvh * G + gg) * n_splits + split) * (SDPA_D + 2);
     dst[2 + dd] = oo;
@@ -307,13 +308,18 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // per (head, split): weight c = exp2(m - M_head) and sum c*l, computed in parallel through
-  // shared memory (the ring is free), then each output dim sums c*o over the splits
-  float* cw = mrg;                 // [G][n_splits] weights
-  float* lsum = mrg + G * n_splits;  // [G]
+  // per (head, split): m and l loaded in one parallel pass into shared memory (the ring is
+  // free), weights c = exp2(m - M_head) and L = sum c*l per head, then every thread sums c*o
+  // for four output dims at once (independent loads in flight)
+  float* cw = mrg;                   // [G][n_splits] m, then weights
+  float* lw = mrg + G * n_splits;    // [G][n_splits] l
+  float* lsum = lw + G * n_splits;   // [G]
   const int64_t bh0 = (int64_t)b * Hq + kvh * G;
   const float* src0 = part + bh0 * n_splits * (SDPA_D + 2);
-  for (int t = threadIdx.x; t < G * n_splits; t += SDPA_THREADS) cw[t] = __ldcg(src0 + (int64_t)t * (SDPA_D + 2));
+  for (int t = threadIdx.x; t < G * n_splits; t += SDPA_THREADS) {
+    cw[t] = __ldcg(src0 + (int64_t)t * (SDPA_D + 2));
+    lw[t] = __ldcg(src0 + (int64_t)t * (SDPA_D + 2) + 1);
+  }
   __syncthreads();
   if (threadIdx.x < G) {
     const int gg = threadIdx.x;
@@ -324,20 +330,37 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
       const float ms = cw[gg * n_splits + s2];
       const float c = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
       cw[gg * n_splits + s2] = c;
-      L += c * __ldcg(src0 + ((int64_t)gg * n_splits + s2) * (SDPA_D + 2) + 1);
+      L += c * lw[gg * n_splits + s2];
     }
     lsum[gg] = L;
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < G * SDPA_D; t += SDPA_THREADS) {
-    const int gg = t / SDPA_D, dd = t % SDPA_D;
-    const float* src = src0 + (int64_t)gg * n_splits * (SDPA_D + 2) + 2 + dd;
-    const float* c = cw + gg * n_splits;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int s2 = 0; s2 < n_splits; s2++) acc = fmaf(c[s2], __ldcg(src + (int64_t)s2 * (SDPA_D + 2)), acc);
-    const float L = lsum[gg];
-    out[(bh0 + gg) * SDPA_D + dd] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+  // thread t sums dims t, t + 128/... of one head: 4 outputs per pass
+  for (int t0 = threadIdx.x; t0 < G * SDPA_D; t0 += 4 * SDPA_THREADS) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* src[4];
+    const float* cws[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int t = min(t0 + j * SDPA_THREADS, G * SDPA_D - 1);
+      const int gg = t / SDPA_D, dd = t % SDPA_D;
+      src[j] = src0 + (int64_t)gg * n_splits * (SDPA_D + 2) + 2 + dd;
+      cws[j] = cw + gg * n_splits;
+    }
+#pragma unroll 4
+    for (int s2 = 0; s2 < n_splits; s2++) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[j] = fmaf(cws[j][s2], __ldcg(src[j] + (int64_t)s2 * (SDPA_D + 2)), acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int t = t0 + j * SDPA_THREADS;
+      if (t < G * SDPA_D) {
+        const int gg = t / SDPA_D, dd = t % SDPA_D;
+        const float L = lsum[gg];
+        out[(bh0 + gg) * SDPA_D + dd] = __float2bfloat16_rn(L > 0.f ? acc[j] / L : 0.f);
+      }
+    }
   }
 }
 
@@ -428,8 +451,8 @@ static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* 
     attr = true;
   }
   const int splits = sdpa_splits(kv_len);
-  // the combining CTA keeps a weight per (head, split) in the 64 KB ring
-  if (splits > 65535 || (size_t)(splits + 1) * (n_heads / n_kv_heads) * sizeof(float) > SDPA_RING)
+  // the combining CTA keeps m and l per (head, split) in the ring
+  if (splits > 65535 || (size_t)(2 * splits + 1) * (n_heads / n_kv_heads) * sizeof(float) > SDPA_RING)
     return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: kv_len=%lld too long", (long long)kv_len);
   const int64_t rows = batch * n_kv_heads * max_len;
   if (rows >= (1LL << 31)) return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: cache of %lld rows", (long long)rows);
@@ -513,7 +536,7 @@ extern "C" int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n,
 //    process has the library loaded on that GPU: 64 KiB of split counters
 //    (zero when the library loads; every call leaves them zero) and the
 //    partials; calls whose partials need more (batch * n_heads *
-//    ceil(kv_len/128) * (head_dim + 2) * 4 bytes) than the rest are rejected
+//    ceil(kv_len/256) * (head_dim + 2) * 4 bytes) than the rest are rejected
 //    with VMLX_E_INVALID;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
