@@ -11,6 +11,8 @@ enum QmvMode : int {
   QMV_SORTED = 2,  // blockIdx.y = expert e: every (b, m) row with rhs[b] == e
 };
 
+constexpr int QMV_TP_MAX_WORLD = 8;  // ranks a fused row-parallel GEMV reduces over
+
 struct QmvArgs {
   const bf16* x;
   const uint32_t* w;
@@ -36,7 +38,7 @@ struct QmvArgs {
   // this rank goes into slot [parity][tp_rank] of every rank's buffer over P2P; each
   // CTA then waits for the same CTA of every rank and reduces its rows in rank order:
   //   y = bf16(residual + bf16(sum_r partial_r)).
-  char* tp_buf[8];  // every rank's TP buffer base, as seen from this device
+  char* tp_buf[QMV_TP_MAX_WORLD];  // every rank's TP buffer base, as seen from this device
   int tp_rank, tp_world;
   size_t tp_slot_bytes;                             // bytes per rank slot
   size_t tp_slots_off, tp_flags_off, tp_epoch_off;  // regions inside each buffer

@@ -786,12 +786,8 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           const int64_t row = I.n0 + rlo + i % nr, tok = i / nr;
           if (row >= p.N) continue;
           const int64_t idx = tok * p.N + row;
-          float sum = 0.f;  // rank order: identical on every rank
-          for (int r = 0; r < p.tp_world && tp_ok; r++) {
-            uint32_t v;
-            tp_ok = wait_ll(slots + r * rstride + idx, tp_e, deadline, v);
-            sum += __bfloat162float(__ushort_as_bfloat16((unsigned short)v));
-          }
+          float sum;  // rank order: identical on every rank
+          tp_ok = wait_ll_sum<QMV_TP_MAX_WORLD>(slots + idx, rstride, p.tp_world, tp_e, deadline, sum);
           if (!tp_ok) break;
           const bf16 sb = __float2bfloat16_rn(sum);
           p.y[idx] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + __bfloat162float(sb)) : sb;

@@ -93,6 +93,36 @@ __device__ __forceinline__ bool wait_ll(const uint64_t* p, uint32_t e, uint64_t 
   }
 }
 
+// Poll world low-latency words (p, p + stride, ...) until each carries epoch e, with
+// every pending load in flight at once: one NVLink/L2 round trip per pass instead of
+// one per word.  Returns the fp32 sum of their bf16 payloads in index (rank) order;
+// false once the deadline passes.
+template <int MAXW>
+__device__ __forceinline__ bool wait_ll_sum(const uint64_t* p, size_t stride, int world, uint32_t e,
+                                            uint64_t deadline_ns, float& sum) {
+  uint32_t pay[MAXW];
+  uint32_t pending = (world >= 32 ? ~0u : (1u << world) - 1u);
+  for (uint32_t it = 0; pending; it++) {
+    uint64_t v[MAXW];
+#pragma unroll
+    for (int r = 0; r < MAXW; r++)
+      if (pending >> r & 1u) v[r] = ld_ll(p + r * stride);
+#pragma unroll
+    for (int r = 0; r < MAXW; r++)
+      if ((pending >> r & 1u) && (uint32_t)(v[r] >> 32) == e) {
+        pay[r] = (uint32_t)v[r];
+        pending &= ~(1u << r);
+      }
+    if (pending && (it & 255) == 255 && globaltimer() > deadline_ns) return false;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < MAXW; r++)
+    if (r < world) s += __bfloat162float(__ushort_as_bfloat16((unsigned short)pay[r]));
+  sum = s;
+  return true;
+}
+
 // Wait until *f - e >= 0 (wrapping 32-bit epochs); false once deadline_ns has passed.
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t e, uint64_t timeout_ns) {
   const uint64_t deadline = globaltimer() + timeout_ns;

@@ -174,15 +174,12 @@ tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const
       st_ll(dst + i, (uint32_t)__bfloat16_as_ushort(in[i]), e);
   }
   const uint64_t deadline = globaltimer() + timeout_ns;
+  const uint64_t* slots = reinterpret_cast<const uint64_t*>(mine + tp_slot_off(parity, 0, max_bytes, world));
+  const size_t rstride = max_bytes / sizeof(uint64_t);
   bool ok = true;
   for (int64_t i = e0 + threadIdx.x; i < e1 && ok; i += TP_THREADS) {
-    float s = 0.f;
-    for (int r = 0; r < world && ok; r++) {
-      uint32_t v;
-      ok = wait_ll(reinterpret_cast<const uint64_t*>(mine + tp_slot_off(parity, r, max_bytes, world)) + i, e,
-                   deadline, v);
-      s += __bfloat162float(__ushort_as_bfloat16((unsigned short)v));
-    }
+    float s;
+    ok = wait_ll_sum<TP_MAX_WORLD>(slots + i, rstride, world, e, deadline, s);
     if (ok) out[i] = __float2bfloat16_rn(s);
   }
   if (!ok) atomicExch(status, VMLX_E_PEER_TIMEOUT);
@@ -308,10 +305,15 @@ extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, v
   ctas = (n + chunk - 1) / chunk;
   TpPeers peers;
   for (int r = 0; r < TP_MAX_WORLD; r++) peers.buf[r] = r < h->world ? h->peer_base[r] : nullptr;
-  if ((size_t)n * 8 <= h->max_bytes)
+  if ((size_t)n * 8 <= h->max_bytes) {
+    // low-latency words: one element per thread where TP_MAX_CTAS CTAs allow it
+    ctas = (n + TP_THREADS - 1) / TP_THREADS;
+    if (ctas > TP_MAX_CTAS) ctas = TP_MAX_CTAS;
+    chunk = (n + ctas - 1) / ctas;
+    ctas = (n + chunk - 1) / chunk;
     tp_all_sum_ll_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
         peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
-  else
+  } else
     tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
         peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
   return check_launch("tp_all_sum_kernel");
