@@ -117,6 +117,21 @@ def dequantize(wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
     return out.reshape(*wq.shape[:-1], K)
 
 
+def dequantize_bf16(wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """bf16 dequantization from bf16 scales, as affine_dequantize computes it with
+    T = bfloat (quantized.h:2498-2560): bf16(bf16(s * q) + b), each operation rounded
+    to nearest even.  Returns bf16 bit patterns."""
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    K = wq.shape[-1] * 32 // bits
+    q = np.zeros(wq.shape[:-1] + (K,), np.float32)
+    per = 32 // bits
+    for j in range(per):
+        q[..., j::per] = ((wq >> (bits * j)) & ((1 << bits) - 1)).astype(np.float32)
+    s = np.repeat(bf16_to_f32(scales), group_size, axis=-1).reshape(q.shape)
+    b = np.repeat(bf16_to_f32(biases), group_size, axis=-1).reshape(q.shape)
+    return f32_to_bf16(round_bf16(s * q) + b)
+
+
 def qmm_f64(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
     """fp64-accumulated y = x @ deq(W)^T; x given as bf16 bit patterns [M, K]."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
@@ -264,3 +279,82 @@ def sdpa_ref(q, k, v, scale):
             p = np.exp(s - s.max())
             out[b, h] = (p / p.sum()) @ vv
     return out
+
+
+# ---- the reference's own kernels, compiled for the CPU (oracle/_ref) ----------------
+# oracle/Makefile `make ref REF_ROOT=<reference checkout>` cuts affine_quantize,
+# affine_dequantize and qmv_fast_impl out of the reference's quantized.h unchanged and
+# compiles them against oracle/ref_shim.h.  These wrappers pin the C restatement above
+# to them.  The library exists only where the reference checkout was available at build
+# time (it then travels with the repository's built files).
+
+REF_LIB = os.path.join(HERE, "_ref", "libmlx_metal_ref.so")
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        h = ctypes.CDLL(REF_LIB)
+        P = ctypes.c_void_p
+        I64 = ctypes.c_int64
+        I = ctypes.c_int
+        h.ref_quantize.argtypes = [P, I, I64, I64, I, I, P, P, P]
+        h.ref_dequantize.argtypes = [P, P, P, I, I64, I64, I, I, P]
+        h.ref_qmv_fast.argtypes = [P, I64, I64, P, P, P, I64, I, I, P]
+        _ref = h
+    return _ref
+
+
+def ref_quantize(w, group_size=64, bits=4, dtype="bf16"):
+    """The reference's affine_quantize: same return convention as quantize()."""
+    w = np.asarray(w)
+    rows, K = w.shape
+    wq = np.zeros((rows, K * bits // 32), np.uint32)
+    ng = K // group_size
+    if dtype == "bf16":
+        wb = np.ascontiguousarray(w if w.dtype == np.uint16 else f32_to_bf16(w))
+        s = np.zeros((rows, ng), np.uint16)
+        b = np.zeros((rows, ng), np.uint16)
+        rc = ref_lib().ref_quantize(_p(wb), 1, rows, K, group_size, bits, _p(wq), _p(s), _p(b))
+    else:
+        wf = np.ascontiguousarray(w, dtype=np.float32)
+        s = np.zeros((rows, ng), np.float32)
+        b = np.zeros((rows, ng), np.float32)
+        rc = ref_lib().ref_quantize(_p(wf), 0, rows, K, group_size, bits, _p(wq), _p(s), _p(b))
+    if rc:
+        raise ValueError(f"reference quantize failed rc={rc}")
+    return wq, s, b
+
+
+def ref_dequantize(wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """The reference's affine_dequantize; returns the output in the scales' dtype
+    (bf16 bit patterns as uint16, or float32)."""
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    rows = wq.shape[0]
+    K = wq.shape[1] * 32 // bits
+    is_bf16 = scales.dtype == np.uint16
+    out = np.zeros((rows, K), np.uint16 if is_bf16 else np.float32)
+    rc = ref_lib().ref_dequantize(_p(wq), _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)),
+                                  int(is_bf16), rows, K, group_size, bits, _p(out))
+    if rc:
+        raise ValueError("reference dequantize failed")
+    return out
+
+
+def ref_qmv_fast(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarray:
+    """The reference's qmv_fast_impl: y bf16 bit patterns [M, N]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    M, K = x.shape
+    N = wq.shape[0]
+    y = np.zeros((M, N), np.uint16)
+    rc = ref_lib().ref_qmv_fast(_p(x), M, K, _p(np.ascontiguousarray(wq, dtype=np.uint32)),
+                                _p(np.ascontiguousarray(scales)), _p(np.ascontiguousarray(biases)), N,
+                                group_size, bits, _p(y))
+    if rc:
+        raise ValueError("reference qmv_fast failed (shape not covered)")
+    return y

@@ -14,10 +14,11 @@
  *     :28-114, :209-316, :799-864  qmv_fast_impl accumulation
  *                                  (scale*sum(x*q) + bias*sum(x) per group)
  *     :1438-1491 adjust_matrix_offsets (gather lhs/rhs index semantics)
- * Parity status: the quantize / dequantize / qmv restatement is checked against
- * the reference's own Metal kernels compiled for the CPU (oracle/_ref, see
- * oracle/Makefile) on the same inputs, and against the known-answer fixture of
- * Tests/MLXTests/QuantizationTests.swift:65-111.
+ * Parity status: quantize and dequantize are bit-exact against the reference's own
+ * affine_quantize / affine_dequantize, and the fp64 qmv agrees with its qmv_fast_impl
+ * within 1e-2, both compiled for the CPU from quantized.h (make -C oracle ref ->
+ * oracle/_ref; tests/test_oracle_ref.py, golden outputs in tests/golden/ref_kernels.npz),
+ * and the known-answer fixture of Tests/MLXTests/QuantizationTests.swift:65-111 holds.
  *
  * Conventions
  *   - bf16 values travel as uint16_t bit patterns; bf16 <- f32 is round to

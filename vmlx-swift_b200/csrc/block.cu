@@ -443,12 +443,9 @@ static size_t sdpa_ws_bytes(int64_t batch, int n_heads, int64_t kv_len) {
 static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
                        int64_t batch,
                        int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    int rc = check_cuda(cudaFuncSetAttribute(sdpa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SDPA_SMEM), "sdpa_decode: cudaFuncSetAttribute");
+  {
+    const int rc = ensure_max_dynamic_smem((const void*)sdpa_decode_kernel, (int)SDPA_SMEM);
     if (rc) return rc;
-    attr = true;
   }
   const int splits = sdpa_splits(kv_len);
   // the combining CTA keeps m and l per (head, split) in the ring

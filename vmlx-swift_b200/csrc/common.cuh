@@ -21,6 +21,12 @@ typedef __nv_bfloat162 bf162;
 int set_error(int code, const char* fmt, ...);
 void clear_error();
 
+// Raises a kernel's dynamic shared-memory limit on the current device (once per
+// kernel and device; thread-safe).
+int ensure_max_dynamic_smem(const void* func, int bytes);
+// Multiprocessor count of the current device.
+int sm_count();
+
 // Programmatic dependent launch of the streaming kernels (vmlx_set_launch_overlap).
 bool launch_overlap();
 

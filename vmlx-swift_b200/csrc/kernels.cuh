@@ -48,6 +48,11 @@ struct QmvArgs {
 
 constexpr int TP_FUSED_MAXC = 1024;  // CTAs of a fused TP GEMV grid (flag slots per rank)
 
+// Streaming decode GEMV for 1..4 token rows (dense mode, no TP); launch_qmv routes
+// the calls it covers to it.
+bool qgemv_covers(const QmvArgs& a, int mode, int bits, int gs);
+int launch_qgemv(const QmvArgs& a, int bits, int gs, cudaStream_t st);
+
 int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int toka, cudaStream_t st);
 
 // tcgen05 GEMM for M > 32; sets *handled = false when the shape is not covered.

@@ -37,7 +37,6 @@ namespace cg = cooperative_groups;
 
 namespace vmlx {
 
-int sm_count();
 
 constexpr int TC_UM = 128;  // UMMA M (weight rows per MMA = TMEM lanes)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row of bf16)
@@ -380,12 +379,9 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
                      int64_t N, int64_t K, cudaStream_t st) {
   using L = TcLayout<BITS, BT, NH>;
   auto kern = qmm_tc_kernel<BITS, GS, BT, NH>;
-  static bool attr = false;
-  if (!attr) {
-    int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM),
-                        "qmm_tc: cudaFuncSetAttribute");
+  {
+    const int rc = ensure_max_dynamic_smem((const void*)kern, (int)L::SMEM);
     if (rc) return rc;
-    attr = true;
   }
   CUtensorMap tmx, tmw;
   if (!make_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TC_BK,

@@ -105,7 +105,13 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const TS* __r
 #pragma unroll
   for (int j = 0; j < PER; j++) {
     float q = (float)((word >> (BITS * j)) & ((1u << BITS) - 1u));
-    out[k0 + j] = from_f32<TO>(__fadd_rn(__fmul_rn(s, q), b));  // unfused, as written in the source
+    // affine_dequantize (quantized.h:2498-2560) computes `scale * d + bias` in the scales'
+    // type T: for T = float that is an unfused fp32 multiply and add; for T = bfloat each
+    // operation rounds to bf16 (round to nearest even), so a bf16 result from bf16
+    // scales rounds the product before the add.  A float result keeps the exact value.
+    float prod = __fmul_rn(s, q);
+    if constexpr (sizeof(TS) == 2 && sizeof(TO) == 2) prod = __bfloat162float(__float2bfloat16_rn(prod));
+    out[k0 + j] = from_f32<TO>(__fadd_rn(prod, b));
   }
 }
 
