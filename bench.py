@@ -6,7 +6,8 @@ Prints ONE JSON line (rank 0).  Workloads:
   gemv    BASELINE config 1: one MLX affine quantized_matmul, x [1,4096] bf16,
           W [4096,4096] 4-bit g64; a step is one call.  32 weight copies are
           rotated (302 MB > 2x L2) so every call streams its weights from HBM.
-  decode   the TP decoder-stack step.
+  decode  BASELINE config 3: a decode step of the 32-block Llama-3-8B-shaped decoder
+          stack (4-bit g64, bf16 KV cache), TP=N over the ranks of the launch.
 The reference arm (--impl reference) times the CPU restatement of the
 reference arithmetic (oracle/libvmlxq_ref.so, OpenMP on all host cores).
 """
@@ -268,9 +269,10 @@ MOE_EXPERT_BYTES = 3 * MOE_F * MOE_H // 2 + 3 * (MOE_F * MOE_H // 64) * 4  # gat
 
 
 def bench_moe(args, torch, vm, dev):
-    """One MoE layer for T tokens: router softmax -> top-8 (precomputed, synthetic logits ~N(0,1)),
-    SwitchGLU over the routed experts (gather_qmm gate||up, SwiGLU, gather_qmm down), and the
-    score-weighted combine.  Bytes = distinct experts routed x their packed weights (the
+    """One MoE layer for T tokens: router softmax -> top-8 of synthetic logits ~N(0,1)
+    (moe_route kernel), the expert sort when T*8 >= 64 (moe_sort), SwitchGLU over the routed
+    experts (gather_qmm gate||up, SwiGLU, gather_qmm down), and the score-weighted combine
+    with the unsort folded in (moe_combine) -- all inside the timed region.  Bytes = distinct experts routed x their packed weights (the
     reference's per-expert weight stream) + activations."""
     hbm, tf, tf_s, peak_src = peaks()
     T = args.tokens
@@ -287,17 +289,15 @@ def bench_moe(args, torch, vm, dev):
         layer = vm.switch_layers.SwitchGLU(gate, up, down)
         layer.ensure_fused_gate_up()
         layers.append(layer)
-    logits = torch.randn(T, MOE_E, device=dev, generator=g)
-    probs = torch.softmax(logits.float(), -1)
-    scores, inds = torch.topk(probs, MOE_K, dim=-1)
-    inds = inds.to(torch.int32)
-    scores = scores.bfloat16()
+    blocks = [vm.switch_layers.Qwen3MoESparseMoeBlock(None, L, MOE_K) for L in layers]
+    logits = torch.randn(T, MOE_E, device=dev, generator=g)  # router logits ~N(0,1), fp32
+    inds, _ = vm.ops.moe_route(logits, MOE_K)
     x = torch.randn(T, MOE_H, device=dev, generator=g).bfloat16()
     distinct = int(torch.unique(inds).numel())
 
     def layer_fn(L, xin):
-        y = L(xin, inds)                                   # [T, k, H]
-        return (y.float() * scores.float().unsqueeze(-1)).sum(1).bfloat16()
+        # routing (softmax + top-8), sort, SwitchGLU and the weighted combine: device kernels
+        return blocks[layers.index(L)](xin, logits)
     outs = [None] * copies
     calls = [(lambda i=i: outs.__setitem__(i, layer_fn(layers[i], x))) for i in range(copies)]
     with ClockSampler(dev.index or 0) as clk:
@@ -397,25 +397,29 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
     x0 = torch.randn(B, cfg.hidden, device=dev, generator=torch.Generator(device=dev).manual_seed(3)).bfloat16()
     x = x0.clone()
     g = dec.capture(x, pos, stream)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
+    # the clock sampler runs from the warm-up through the GEMV-only timing below, so the line
+    # carries its own samples even when the timed steps last less than one sampling period
+    clk = ClockSampler(dev.index or 0).__enter__()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
             g.replay()
         stream.synchronize()
         if world > 1:
             torch.distributed.barrier()
-        with ClockSampler(dev.index or 0) as clk:
-            e0.record(stream)
-            for _ in range(args.steps):
-                g.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-    t_step = e0.elapsed_time(e1) / 1e3 / args.steps
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        for i in range(args.steps):
+            g.replay()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    per_step = [ev[i].elapsed_time(ev[i + 1]) / 1e3 for i in range(args.steps)]
+    t_mean = ev[0].elapsed_time(ev[-1]) / 1e3 / args.steps
+    t_step = statistics.median(per_step)  # the reference's statistic (median of the steps)
     if world > 1:
-        t = torch.tensor([t_step], device=dev, dtype=torch.float64)
+        t = torch.tensor([t_step, t_mean], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        t_step = t.item()
+        t_step, t_mean = t[0].item(), t[1].item()
     nbytes = decode_step_bytes(dec, pos)
 
     # dominant kernel: the quantized GEMV; time the step's GEMVs alone (same weights, same graph style)
@@ -436,18 +440,39 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
             tp_calls += [lambda L=L: grp.quantized_matmul_all_sum(dec.attn.view(B, -1), L.o, residual=racc, out=racc),
                          lambda L=L: grp.quantized_matmul_all_sum(dec.act, L.down, residual=racc, out=racc)]
         t_tp = time_graph_calls(torch, tp_calls, 5, 3, stream)
-        t = torch.tensor([t_tp], device=dev, dtype=torch.float64)
+        # the same step through the plain GEMV + the unfused P2P all_sum + add, and with NCCL
+        # all_reduce (the baseline the fused kernel replaces), graph-captured alike
+        part = torch.empty(B, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        unf_calls, nccl_calls = [], []
+        for L in dec.layers:
+            for (xin, lin) in ((dec.attn.view(B, -1), L.o), (dec.act, L.down)):
+                unf_calls += [lambda xin=xin, lin=lin: lin(xin, out=part),
+                              lambda: grp.all_sum(part, out=part),
+                              lambda: racc.add_(part)]
+                nccl_calls += [lambda xin=xin, lin=lin: lin(xin, out=part),
+                               lambda: torch.distributed.all_reduce(part),
+                               lambda: racc.add_(part)]
+        t_unf = time_graph_calls(torch, unf_calls, 5, 3, stream) * 3
+        try:
+            t_nccl = time_graph_calls(torch, nccl_calls, 5, 3, stream) * 3
+        except Exception:  # NCCL graph capture unavailable: time it eagerly
+            t_nccl = None
+        t = torch.tensor([t_tp, t_unf, t_nccl or 0.0], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        t_tp = t.item()
+        t_tp, t_unf, t_nccl = t[0].item(), t[1].item(), (t[2].item() or None)
         w_tp = sum(L.o.nbytes + L.down.nbytes for L in dec.layers) / len(tp_calls)
         link = (world - 1) * B * cfg.hidden * 2  # bf16 partial rows sent to the other ranks per call
         t_target = max(w_tp / (hbm * 1e9), link / 770e9)
         tp_fused = {"kernel": "qmv_kernel with the row-parallel all-reduce (vmlx_tp_quantized_matmul_all_sum)",
                     "us_per_call": round(t_tp * 1e6, 2), "weight_bytes_per_call": int(w_tp),
                     "nvlink_bytes_out_per_call": link,
+                    "unfused_us_per_call": round(t_unf * 1e6, 2),
+                    "nccl_us_per_call": round(t_nccl * 1e6, 2) if t_nccl else None,
+                    "nccl_baseline": "quantized GEMV + torch.distributed.all_reduce (NCCL) + residual add",
                     "roofline_us": round(t_target * 1e6, 2), "frac_of_combined_roofline": round(t_target / t_tp, 4),
                     "roofline_basis": "max(weight bytes / measured HBM, NVLink bytes / 770 GB/s measured peer copy)"}
 
+    clk.__exit__(None, None, None)
     # end to end through the public API: host token state in, host state out, every step
     xh = x0.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -462,7 +487,8 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
     res = {
         "metric": "decode tokens/s (Llama-3-8B-shaped decoder, 4-bit g64, TP=N)",
         "value": round(B / t_step, 2), "unit": "tokens/s", "higher_is_better": True,
-        "ms_per_step": t_step * 1e3, "dtype": "bf16",
+        "ms_per_step": t_step * 1e3, "ms_per_step_mean": round(t_mean * 1e3, 4), "step_statistic": "median",
+        "dtype": "bf16",
         "config": {"workload": f"BASELINE config 3: {cfg.n_layers} Llama-3-8B-shaped blocks (hidden 4096, "
                                f"32 Q / 8 KV heads, hd 128, FFN 14336, 4-bit g64), batch {B}, bf16 KV cache of "
                                f"{ctx} random tokens, TP={world}",
@@ -474,7 +500,7 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
         "roofline": {"bound": "hbm", "kernel": "qmv_kernel (decode GEMV)", "achieved": round(gemv_achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(gemv_achieved / hbm, 4), "peak_source": peak_src,
                      "frac_of_8TBps": round(gemv_achieved / 8000, 4),
-                     "traffic": load_traffic(f"qmv_decode_B{B}"),
+                     "traffic": load_traffic(f"qmv_decode_B{B}_tp{world}"),
                      "algorithmic_bytes_per_launch": int(gemv_bytes_avg), "us_per_launch": round(t_gemv * 1e6, 2)},
         "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
                 "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2},

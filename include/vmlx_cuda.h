@@ -85,10 +85,11 @@ VMLX_API int vmlx_cuda_quantize(void* wq, void* scales, void* biases, const void
                        void* stream);
 
 /*
- * Affine dequantization: out[r, k] = scale*q + bias, computed in fp32 as an
- * unfused multiply then add (exact product for bf16 scales) and stored as out_dtype (VMLX_F32: exact; VMLX_BF16: round to nearest even).
- * Replaces mlx_dequantize (Source/Cmlx/include/mlx/c/ops.h:359-369);
- * arithmetic of affine_dequantize (quantized.h:2498-2558).
+ * Affine dequantization: out[r, k] = scale*q + bias as affine_dequantize computes it
+ * (quantized.h:2498-2560): with out_dtype VMLX_F32 an unfused fp32 multiply and add
+ * (exact); with out_dtype VMLX_BF16 from bf16 scales the reference's bfloat
+ * arithmetic, bf16(bf16(scale*q) + bias), each step rounded to nearest even.
+ * Replaces mlx_dequantize (Source/Cmlx/include/mlx/c/ops.h:359-369).
  * scales_dtype gives the dtype of scales/biases.
  */
 VMLX_API int vmlx_cuda_dequantize(void* out, int out_dtype, const uint32_t* wq, const void* scales,
@@ -144,7 +145,9 @@ VMLX_API int vmlx_cuda_quantized_matmul_swiglu(void* y, const void* gate_up, con
  *               b*x_batches/batch), the row-major broadcast of x [T,1,..]
  *               against indices [T,k] that SwitchGLU relies on
  *               (quantized.h:1438-1491); batch must be a multiple of x_batches.
- *   rhs_indices u32 [batch]  expert of each batch element
+ *   rhs_indices u32 [batch]  expert of each batch element, or NULL: batch element b
+ *                 uses expert b * n_experts / batch (batch a multiple of n_experts),
+ *                 MLX's broadcast of the weight stack when no indices are given
  *   y        bf16 [batch, M, N];  y[b] = x[lhs[b]] @ dequantize(w[rhs[b]])^T
  * sorted_indices = true promises rhs_indices is non-decreasing (the
  * gatherSort'ed order, SwitchLayers.swift:64-75); the kernel then streams each
@@ -156,6 +159,47 @@ VMLX_API int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, con
                          const uint32_t* rhs_indices, bool transpose, int group_size, int bits,
                          const char* mode, bool sorted_indices, int64_t batch, int64_t x_batches,
                          int64_t M, int64_t N, int64_t K, int64_t n_experts, void* stream);
+
+
+/* ---- MoE routing around SwitchGLU ---- */
+
+/*
+ * Top-k routing of a sparse MoE block (Qwen3MoESparseMoeBlock.callAsFunction,
+ * Libraries/MLXLLM/Models/Qwen3MoE.swift:137-148):
+ *   soft = softmax(logits, precise)  (fp32 math, stored in the logits' dtype)
+ *   indices[r, :] = the k experts with the largest logits (descending logit, lower
+ *                   id first on ties -- argPartition leaves the order open)
+ *   scores[r, :]  = soft at those experts, divided by their sum if norm_topk_prob
+ * logits [rows, n_experts] of dtype VMLX_F32 or VMLX_BF16; scores have the same dtype.
+ * n_experts <= 1024, k <= 32.
+ */
+VMLX_API int vmlx_cuda_moe_route(const void* logits, int dtype, int64_t rows, int n_experts, int k,
+                                 bool norm_topk_prob, uint32_t* indices, void* scores, void* stream);
+
+/*
+ * gatherSort (Libraries/MLXLMCommon/SwitchLayers.swift:64-75) of the flattened
+ * routing indices [pairs] (pairs = tokens * k): a stable sort by expert id.
+ *   sorted_indices[p] = expert id of sorted pair p           (indices[order])
+ *   lhs_indices[p]    = token row of sorted pair p            (order / k) -- pass to
+ *                       vmlx_cuda_gather_qmm as lhs_indices instead of gathering x
+ *   inverse_order[i]  = sorted position of input pair i       (argSort(order))
+ * n_experts <= 1024.  An id >= n_experts sets *status (if given) to VMLX_E_INVALID.
+ */
+VMLX_API int vmlx_cuda_moe_sort(const uint32_t* indices, int64_t pairs, int k, int n_experts,
+                                uint32_t* sorted_indices, uint32_t* lhs_indices, uint32_t* inverse_order,
+                                int* status, void* stream);
+
+/*
+ * scatterUnsort + the weighted sum of the MoE block (SwitchLayers.swift:77-83,
+ * Qwen3MoE.swift:150-151):
+ *   out[t, :] = sum_j y[src(t, j), :] * scores[t, j],  src = inverse_order[t*k + j]
+ *               (or t*k + j when inverse_order is NULL: y not sorted)
+ * y bf16 [rows*k, dims]; scores [rows, k] VMLX_BF16 (each product rounded to bf16, as
+ * the reference's bf16 multiply) or VMLX_F32 (products kept in fp32); the sum over j
+ * is fp32 and out bf16 [rows, dims].  dims a multiple of 8, rows <= 65535.
+ */
+VMLX_API int vmlx_cuda_moe_combine(const void* y, const uint32_t* inverse_order, const void* scores,
+                                   int scores_dtype, int64_t rows, int k, int64_t dims, void* out, void* stream);
 
 
 /* ---- decoder-block support kernels (bf16) ---- */

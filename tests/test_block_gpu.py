@@ -111,10 +111,11 @@ def _layer_ref(orc, dec, x, pos):
     return x
 
 
-@pytest.mark.parametrize("fused", [False, True])
-def test_decoder_step_matches_reference(vm, orc, cuda, fused):
+@pytest.mark.parametrize("fused,B", [(False, 3), (True, 3), (False, 16), (True, 16), (True, 64)])
+def test_decoder_step_matches_reference(vm, orc, cuda, fused, B):
+    """BASELINE config 3 batches (1/16/64; B=64 runs the tensor-core GEMM for every linear)."""
     cfg = vm.llama.LlamaConfig(hidden=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1024, n_layers=2)
-    B, pos = 3, 64
+    pos = 64
     dec = vm.llama.LlamaDecoder(cfg, B, max_len=96, dev=cuda, seed=5, cache_fill=pos, fused=fused)
     g = torch.Generator(cuda).manual_seed(9)
     x = torch.randn(B, cfg.hidden, device=cuda, generator=g).bfloat16()

@@ -184,6 +184,19 @@ def _tp_worker(rank, world, port, q):
         torch.cuda.synchronize()
         once = row(xl, fused=False)
         ok.append(torch.equal(outb, vm.fast.add(once, once)))
+        # MoE (config 4 layout, reduced): experts' intermediate sharded over the group, the block's
+        # partial outputs all-reduced, against the unsharded SwitchGLU + combine on this GPU
+        E, D, F = 8, 512, 768
+        gen = torch.Generator().manual_seed(21)
+        mk = lambda n, kk: vm.switch_layers.QuantizedSwitchLinear.from_weight(  # noqa: E731
+            (torch.randn(E, n, kk, generator=gen) * 0.02).bfloat16().to(dev))
+        glu = vm.SwitchGLU(mk(F, D), mk(F, D), mk(D, F))
+        xm = torch.randn(5, D, generator=gen).bfloat16().to(dev)
+        lg = torch.randn(5, E, generator=gen).to(dev)
+        inds, scores = vm.ops.moe_route(lg, 2)
+        full_m = glu.combined(xm, inds, scores).float()
+        part_m = vm.distributed.ShardedSwitchGLU(glu, grp).combined(xm, inds, scores).float()
+        ok.append(((part_m - full_m).abs().max() / full_m.abs().max()).item() <= 2e-2)
         ok.append(grp.status() == 0)
         q.put((rank, ok, rel))
         grp.close()

@@ -9,6 +9,8 @@ from ._lib import VMLXError, build, lib  # noqa: F401
 from . import ops, nn, switch_layers  # noqa: F401
 from .ops import dequantized, gather_quantized_mm, quantized, quantized_mm  # noqa: F401
 from .nn import QuantizedLinear  # noqa: F401
-from .switch_layers import QuantizedSwitchLinear, SwitchGLU, gather_sort, scatter_unsort  # noqa: F401
+from .switch_layers import (QuantizedSwitchLinear, SwitchGLU, Qwen3MoESparseMoeBlock, gather_sort,  # noqa: F401
+                            scatter_unsort)
+from .ops import moe_combine, moe_route, moe_sort  # noqa: F401
 from . import fast, llama  # noqa: F401,E402
 from . import distributed  # noqa: F401,E402

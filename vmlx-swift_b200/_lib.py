@@ -47,6 +47,9 @@ SIGNATURES = {
     "vmlx_cuda_gather_qmm": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _bool, _int, _int, _str, _bool, _i64, _i64,
                _i64, _i64, _i64, _i64, _vp]),
+    "vmlx_cuda_moe_route": (_int, [_vp, _int, _i64, _int, _int, _bool, _vp, _vp, _vp]),
+    "vmlx_cuda_moe_sort": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
+    "vmlx_cuda_moe_combine": (_int, [_vp, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp]),
     "vmlx_cuda_rms_norm": (_int, [_vp, _vp, _vp, _c.c_float, _i64, _i64, _vp]),
     "vmlx_cuda_rope_qkv": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _c.c_float,
                                   _c.c_float, _vp]),

@@ -53,7 +53,9 @@ extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, c
                                     int64_t n_experts, void* stream) {
   int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
   if (rc) return rc;
-  if (!rhs_indices) return set_error(VMLX_E_INVALID, "rhs_indices is required");
+  if (!rhs_indices && batch % n_experts)
+    return set_error(VMLX_E_INVALID, "without rhs_indices, batch=%lld must be a multiple of n_experts=%lld",
+                     (long long)batch, (long long)n_experts);
   if (batch < 0 || x_batches <= 0 || n_experts <= 0)
     return set_error(VMLX_E_INVALID, "bad batch=%lld x_batches=%lld n_experts=%lld", (long long)batch,
                      (long long)x_batches, (long long)n_experts);
@@ -64,7 +66,7 @@ extern "C" int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, c
   QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, lhs_indices,
             rhs_indices, M, N, K, batch, x_batches, n_experts};
   cudaStream_t st = as_stream(stream);
-  if (sorted_indices) {
+  if (sorted_indices && rhs_indices) {
     // rows per expert on average, staged in passes of up to 32 rows
     int64_t avg = (batch * M + n_experts - 1) / n_experts;
     int toka = (int)((avg + avg / 2 + 7) / 8 * 8);

@@ -6,27 +6,31 @@
 // fusions of the other GEMV kernel (RMSNorm of x on load, SwiGLU of a gate||up x on
 // load, residual add on store).
 //
-// B200 design.  At 0.5625 B per 4-bit weight the op is a pure HBM stream, so the
-// kernel is organised around keeping many bytes in flight on every SM with as few
-// instructions per weight as possible:
-//  * Every warp streams its own weights: lane 0 keeps QG_STAGES TMA loads
-//    (cp.async.bulk.tensor.2d, 16 rows x 128 bytes, 128-byte swizzle, no multicast)
-//    in flight into a warp-private shared-memory ring, each completing on its own
-//    mbarrier.  The bytes in flight per SM are set by the ring, not by registers
-//    (3 stages x 2 KB x 24 warps), which is what an HBM stream with microsecond
-//    latency needs; there is no producer warp and no cross-warp handshake.
-//  * A warp owns a 16-row strip and a contiguous range of groups; the CTA's 8 warps
-//    are S strips x (8/S) group ranges; a thread-block cluster of C CTAs splits K
-//    further.  Partial tiles are added in a fixed order (warps through shared memory,
-//    cluster CTAs through distributed shared memory): deterministic, no atomics, no
-//    global scratch.
-//  * The dot products run on mma.sync.m16n8k16: A = the 16 rows' codes as exact bf16
-//    128+q (one shift and one lop3 per two 4-bit codes, no rounding), B = x in the
-//    matching k order, tokens as the MMA's N dimension.  Per group the fold is
-//    scale*sum(x*(128+q)) + (bias - 128*scale)*sum(x), the factorisation of MLX's qdot
-//    (quantized.h:209-316); the per-group sums of x are computed once per CTA.
-//  * x (after the optional RMSNorm / SwiGLU) is staged once per CTA in shared memory,
-//    permuted inside each 8-value block to the order the unpack produces codes in.
+// B200 design.  At 0.5625 B per 4-bit weight the op is a pure HBM stream; the kernel
+// keeps bytes in flight on every SM for the whole call and spends few instructions per
+// weight:
+//  * Persistent CTAs (as many as are resident), each looping over row tiles of 16*S
+//    rows.  Every warp streams its own weights: lane 0 keeps QG_STAGES TMA loads
+//    (cp.async.bulk.tensor.2d, 16 rows x 128 bytes, 128-byte swizzle, no multicast) in
+//    flight into a warp-private shared-memory ring, each completing on its own
+//    mbarrier, and the ring runs ahead across tile boundaries -- no producer warp, no
+//    cross-warp handshake, no refill gap between tiles.
+//  * A tile's 16*S rows are split over the CTA's 8 warps as S strips x (8/S) group
+//    ranges; a thread-block cluster of C CTAs splits K further.  Partial tiles are
+//    added in a fixed order (warps through shared memory, cluster CTAs through
+//    distributed shared memory): deterministic, no atomics, no global scratch.
+//  * The next tile's bf16 scales and biases are copied into shared memory with
+//    cp.async while the current tile is computed (double buffer, padded rows so the
+//    8 rows a warp reads at once fall in different banks).
+//  * The dot products run on mma.sync.m16n8k16 in fp16 with fp32 accumulation:
+//    A = the 16 rows' codes as exact fp16 values 1024+q (4-bit odd nibbles 1024+16q),
+//    built with one prmt and four lop3 per 8 codes; B = x in the matching k order,
+//    tokens as the MMA's N dimension.  x is staged once per CTA, each token scaled by a
+//    power of two 2^s (max |x| 2^s < 2^15, so fp16 holds every bf16 value exactly) and
+//    the odd-nibble positions by a further 2^-4; per group the fold is
+//    scale * (sum(x' code) - 1024 sum(x')) * 2^-s + bias * sum(x), the factorisation of
+//    MLX's qdot (quantized.h:209-316).  Power-of-two scaling commutes with rounding, so
+//    the result does not depend on s.
 // The CTA geometry depends on (N, K, bits, group size) only, never on M, so a row's
 // result is the same whether it is computed alone or with up to 3 other rows (batch
 // invariance, QuantizedSmallMScalingBenchTests.swift:110-127).
@@ -37,6 +41,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace vmlx {
 
 namespace cg = cooperative_groups;
@@ -46,7 +52,7 @@ constexpr int QG_THREADS = 32 * QG_WARPS;
 constexpr int QG_MAXM = 4;        // token rows of this regime
 constexpr int QG_MAX_CLUSTER = 8;
 constexpr int QG_TOKP = 8;        // token slots of an MMA tile (N dimension)
-constexpr int QG_STAGES = 3;      // default ring stages per warp
+constexpr int QG_STAGES = 3;      // ring stages per warp
 constexpr int QG_STAGE_BYTES = 16 * 128;  // one stage: 16 rows x 128 bytes
 
 template <int BITS, int GS>
@@ -58,55 +64,51 @@ struct QGT {
 };
 
 struct QgGeom {
-  int S;      // 16-row strips per CTA
-  int C;      // CTAs per cluster (K split)
-  int KGC;    // groups per CTA
-  int GW;     // groups per warp
-  int xstr;   // bytes per staged x row
-  int sbstr;  // 32-bit words per staged (scale, bias) row
-  int sc_vec;  // scales/biases rows load as 16-byte vectors
-  int D;       // ring stages per warp
-  int dbg;
+  int S;         // 16-row strips per tile
+  int C;         // CTAs per cluster (K split)
+  int KGC;       // groups per CTA
+  int GW;        // groups per warp (a whole number of ring stages)
+  int xstr;      // bytes per staged x row
+  int sbrow;     // bytes per staged scale (or bias) row: 16-byte multiple + 16 of padding
+  int ntiles;    // row tiles of 16*S rows
+  int sc_async;  // scales/biases rows are 16-byte aligned: cp.async them
 };
 
 struct QgSmem {
-  size_t o_ring, o_bar, o_xs, o_xsum, o_sb, o_red, o_ctile, total;
+  size_t o_ring, o_bar, o_xs, o_xsum, o_sc, o_red, o_ctile, total;
   __host__ __device__ void init(const QgGeom& g, int m) {
     o_ring = 0;  // 1024-byte aligned (the swizzle atom)
-    o_bar = o_ring + (size_t)QG_WARPS * g.D * QG_STAGE_BYTES;
-    o_xs = o_bar + (size_t)QG_WARPS * g.D * 8;
+    o_bar = o_ring + (size_t)QG_WARPS * QG_STAGES * QG_STAGE_BYTES;
+    o_xs = o_bar + (size_t)QG_WARPS * QG_STAGES * 8;
     o_xsum = o_xs + (size_t)m * g.xstr;
-    o_sb = o_xsum + (size_t)2 * g.KGC * QG_TOKP * 4;
-    o_red = o_sb + (size_t)16 * g.S * g.sbstr * 4;
+    o_sc = o_xsum + (size_t)2 * g.KGC * QG_TOKP * 4;
+    o_red = o_sc + (size_t)2 * 2 * 16 * g.S * g.sbrow;  // [buffer][scale | bias][row]
     o_ctile = o_red + (size_t)QG_WARPS * 16 * QG_TOKP * 4;
     total = o_ctile + (g.C > 1 ? (size_t)16 * g.S * QG_TOKP * 4 : 0) + 1024;  // + alignment slack
   }
 };
 
-// LB bytes of row r (0..15) at byte o of a 128-byte-swizzled [16][128] stage:
+// Byte offset of (row r in 0..15, byte o) in a 128-byte-swizzled [16][128] stage:
 // 16-byte chunk j of row r sits at chunk j ^ (r & 7).
+__device__ __forceinline__ int swz(int r, int o) { return r * 128 + ((((o >> 4) ^ (r & 7))) << 4) + (o & 15); }
+
 template <int LB>
-__device__ __forceinline__ void lds_lane(const uint8_t* stg, int r, int o, uint32_t (&w)[LB / 4]) {
-#pragma unroll
-  for (int h = 0; h < (LB + 15) / 16; h++) {
-    const int oo = o + 16 * h;
-    const uint8_t* a = stg + r * 128 + ((((oo >> 4) ^ (r & 7))) << 4) + (oo & 15);
-    if constexpr (LB == 4) {
-      w[0] = *reinterpret_cast<const uint32_t*>(a);
-    } else if constexpr (LB == 8) {
-      const uint2 v = *reinterpret_cast<const uint2*>(a);
-      w[0] = v.x; w[1] = v.y;
-    } else {
-      const uint4 v = *reinterpret_cast<const uint4*>(a);
-      w[4 * h] = v.x; w[4 * h + 1] = v.y; w[4 * h + 2] = v.z; w[4 * h + 3] = v.w;
-    }
+__device__ __forceinline__ void lds_lane(const uint8_t* a, uint32_t (&w)[LB / 4]) {
+  if constexpr (LB == 4) {
+    w[0] = *reinterpret_cast<const uint32_t*>(a);
+  } else if constexpr (LB == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(a);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(a);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
   }
 }
 
 // 4-bit word -> four fp16 pairs, exact: p[0] = (n0, n4) + 1024, p[1] = 16 (n1, n5) + 1024,
-// p[2] = (n2, n6) + 1024, p[3] = 16 (n3, n7) + 1024 (the fp16 exponent 0x64 makes the
-// low 10 bits integer mantissa, so a masked nibble at bits 0-3 or 4-7 of each half is
-// read as itself or 16x itself).  Four lop3 and one prmt per 8 codes, no shifts.
+// p[2] = (n2, n6) + 1024, p[3] = 16 (n3, n7) + 1024 (under the fp16 exponent byte 0x64
+// the low 10 bits are an integer mantissa, so a nibble masked at bits 0-3 or 4-7 of a
+// half reads as itself or 16x itself).  One prmt and four lop3 per 8 codes.
 __device__ __forceinline__ void unpack4h(uint32_t w, uint32_t (&p)[4]) {
   const uint32_t E = 0x64006400u;
   const uint32_t w2 = prmt(w, 0u, 0x3311);  // bytes (b1, b1, b3, b3)
@@ -116,8 +118,8 @@ __device__ __forceinline__ void unpack4h(uint32_t w, uint32_t (&p)[4]) {
   p[3] = (w2 & 0x00F000F0u) | E;
 }
 
-// 8-bit word (4 codes) -> two fp16 pairs (q0, q1) + 1024, (q2, q3) + 1024: the code byte
-// becomes the low mantissa byte under an 0x64 exponent byte.
+// 8-bit word (4 codes) -> (q0, q1) + 1024, (q2, q3) + 1024: the code byte becomes the
+// low mantissa byte under an 0x64 exponent byte.
 __device__ __forceinline__ void unpack8h(uint32_t w, uint32_t (&p)[2]) {
   p[0] = prmt(w, 0x64646464u, 0x4140);
   p[1] = prmt(w, 0x64646464u, 0x4342);
@@ -132,12 +134,56 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Scales and biases of the tile at row0 (the CTA's groups cg0..cg0+ncg) into buffer
+// `dst` ([scale | bias][16*S rows][sbrow bytes]).  Asynchronous (cp.async; one commit
+// group per call, empty when !valid) when rows are 16-byte aligned, else plain loads.
+__device__ __forceinline__ void qg_load_scales(const QmvArgs& p, const QgGeom& g, uint8_t* dst, int64_t row0,
+                                               int64_t KG, int64_t cg0, int ncg, bool valid, int tid) {
+  const int rows = 16 * g.S;
+  if (valid) {
+    if (g.sc_async) {
+      const int nchunk = (ncg + 7) >> 3;  // 8 groups per 16-byte chunk (KGC is a multiple of 8)
+      for (int i = tid; i < 2 * rows * nchunk; i += QG_THREADS) {
+        const int kind = i / (rows * nchunk), rem = i - kind * rows * nchunk;
+        const int r = rem / nchunk, ch = rem - r * nchunk;
+        const int64_t row = row0 + r < p.N ? row0 + r : p.N - 1;
+        const bf16* src = (kind ? p.biases : p.scales) + row * KG + cg0 + ch * 8;
+        cp_async16(dst + ((size_t)kind * rows + r) * g.sbrow + ch * 16, src);
+      }
+    } else {
+      for (int i = tid; i < 2 * rows * ncg; i += QG_THREADS) {
+        const int kind = i / (rows * ncg), rem = i - kind * rows * ncg;
+        const int r = rem / ncg, gl = rem - r * ncg;
+        const int64_t row = row0 + r < p.N ? row0 + r : p.N - 1;
+        reinterpret_cast<bf16*>(dst + ((size_t)kind * rows + r) * g.sbrow)[gl] =
+            (kind ? p.biases : p.scales)[row * KG + cg0 + gl];
+      }
+    }
+  }
+  cp_async_commit();
+}
+
+#ifdef QG_X_TRACE
+__device__ unsigned long long qg_trace[8];
+extern "C" int vmlx_qg_trace(unsigned long long* out, int reset) {
+  cudaMemcpyFromSymbol(out, qg_trace, sizeof(qg_trace));
+  if (reset) { unsigned long long z[8] = {0, 0, 0, 0, 0, ~0ull, 0, 0}; cudaMemcpyToSymbol(qg_trace, z, sizeof(z)); }
+  return 0;
+}
+#endif
 template <int BITS, int GS>
 __global__ void __launch_bounds__(QG_THREADS, 3)
 qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   using T = QGT<BITS, GS>;
   constexpr int LB = T::LB, WL = T::WL, GB = T::GB, GC = T::GC;
   constexpr int BPG = GS / 8;  // 8-value x blocks per group
+  constexpr int NH = (LB + 15) / 16, LBH = LB < 16 ? LB : 16;  // 16-byte pieces of a lane's slice
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   __shared__ float xinv[QG_MAXM];    // fused RMSNorm: 1 / rms per token
@@ -149,97 +195,60 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   const int S = g.S, C = g.C;
   const int M = (int)p.M;
   const int crank = C > 1 ? (int)(blockIdx.x % C) : 0;
-  const int64_t row_base = (int64_t)(blockIdx.x / C) * 16 * S;
+  const int64_t cluster_id = blockIdx.x / C, nclusters = gridDim.x / C;
   const int64_t KG = p.K / GS;
   const int64_t cg0 = (int64_t)crank * g.KGC;
   const int ncg = (int)(KG - cg0 < g.KGC ? (KG - cg0 > 0 ? KG - cg0 : 0) : g.KGC);
   const int s = warp % S, ksub = warp / S;
   const int wg0 = ksub * g.GW;
   const int nwg = ncg - wg0 < g.GW ? (ncg - wg0 > 0 ? ncg - wg0 : 0) : g.GW;
+  const int nch = (nwg + GC - 1) / GC;  // ring stages per tile for this warp
+  const int64_t ntl = cluster_id < g.ntiles ? (g.ntiles - 1 - cluster_id) / nclusters + 1 : 0;
+  const int total_st = (int)(ntl * nch);
+  const int rows = 16 * S;
 
   QgSmem L;
   L.init(g, M);
   uint8_t* xs = smem + L.o_xs;
-  float* xsumb = reinterpret_cast<float*>(smem + L.o_xsum);       // [g][t] sum of x
-  float* xsumq = xsumb + (size_t)g.KGC * QG_TOKP;                 // [g][t] 1024 * sum of staged x
-  uint32_t* sb = reinterpret_cast<uint32_t*>(smem + L.o_sb);
+  float* xsumb = reinterpret_cast<float*>(smem + L.o_xsum);  // [g][t] sum of x
+  float* xsumq = xsumb + (size_t)g.KGC * QG_TOKP;              // [g][t] 1024 * sum of staged x
   float* red = reinterpret_cast<float*>(smem + L.o_red);
   float* ctile = reinterpret_cast<float*>(smem + L.o_ctile);
-  const int D = g.D;
-  uint8_t* ring = smem + L.o_ring + (size_t)warp * D * QG_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.o_bar) + warp * D;
+  uint8_t* ring = smem + L.o_ring + (size_t)warp * QG_STAGES * QG_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.o_bar) + warp * QG_STAGES;
+  const size_t scbuf = (size_t)2 * rows * g.sbrow;
 
   // Weights and scales are static: start streaming them before waiting on the
   // previous kernel (programmatic dependent launch), and let the next kernel launch.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int nch = (nwg + GC - 1) / GC;  // ring stages of this warp
-  const int wrow = (int)(row_base + s * 16);
-  const int wx0 = (int)((cg0 + wg0) * GB);
+#ifdef QG_X_TRACE
+  const uint64_t t_start = globaltimer();
+#endif
   if (lane == 0) {
-    for (int d = 0; d < D; d++) mbar_init(&bars[d], 1);
+    for (int d = 0; d < QG_STAGES; d++) mbar_init(&bars[d], 1);
     fence_mbar_init();
   }
   __syncwarp();
+  // stage j of this warp: tile j / nch, group range (j % nch) * GC of the warp's range
+  // The next stage to load: tile iss_row (first row of the warp's strip in it) and group
+  // column iss_x; advanced incrementally (lane 0 only), no divisions on the issue path.
+  int iss_jj = 0, iss_row = (int)(cluster_id * rows + s * 16);
+  const int row_step = (int)(nclusters * rows);
+  const int x0 = (int)((cg0 + wg0) * GB);
+  auto issue = [&](int st) {
+    mbar_arrive_expect_tx(&bars[st], QG_STAGE_BYTES);
+    tma_load_2d(ring + st * QG_STAGE_BYTES, &tmw, x0 + iss_jj * (GC * GB), iss_row, &bars[st]);
+    if (++iss_jj == nch) {
+      iss_jj = 0;
+      iss_row += row_step;
+    }
+  };
   if (lane == 0) {
     tma_prefetch_desc(&tmw);
-    for (int j = 0; j < nch && j < D; j++) {
-      mbar_arrive_expect_tx(&bars[j], QG_STAGE_BYTES);
-      tma_load_2d(ring + j * QG_STAGE_BYTES, &tmw, wx0 + j * GC * GB, wrow, &bars[j]);
-    }
+    for (int j = 0; j < total_st && j < QG_STAGES; j++) issue(j);
   }
-
-  // (scale, bias) of the CTA's rows and groups as bf16 pairs.  Items are (row, octet of
-  // 8 groups); each thread issues the loads of up to 4 items before storing any, so the
-  // staging costs one memory latency rather than one per item.
-  {
-    const int noct = (ncg + 7) >> 3;
-    const int items = 16 * S * noct;
-    const bool vec = g.sc_vec;
-    for (int base = 0; base < items; base += 4 * QG_THREADS) {
-      uint4 sv[4], bv[4];
-#pragma unroll
-      for (int b = 0; b < 4; b++) {
-        const int i = base + b * QG_THREADS + tid;
-        sv[b] = bv[b] = make_uint4(0, 0, 0, 0);
-        if (i < items) {
-          const int r = i / noct, o8 = (i - r * noct) * 8;
-          const int64_t row = row_base + r < p.N ? row_base + r : p.N - 1;
-          const bf16* sp = p.scales + row * KG + cg0 + o8;
-          const bf16* bp = p.biases + row * KG + cg0 + o8;
-          if (vec) {
-            sv[b] = *reinterpret_cast<const uint4*>(sp);
-            bv[b] = *reinterpret_cast<const uint4*>(bp);
-          } else {
-            uint16_t ts[8], tb[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-              ts[e] = o8 + e < ncg ? __bfloat16_as_ushort(sp[e]) : 0;
-              tb[e] = o8 + e < ncg ? __bfloat16_as_ushort(bp[e]) : 0;
-            }
-            sv[b] = make_uint4(ts[0] | (uint32_t)ts[1] << 16, ts[2] | (uint32_t)ts[3] << 16,
-                               ts[4] | (uint32_t)ts[5] << 16, ts[6] | (uint32_t)ts[7] << 16);
-            bv[b] = make_uint4(tb[0] | (uint32_t)tb[1] << 16, tb[2] | (uint32_t)tb[3] << 16,
-                               tb[4] | (uint32_t)tb[5] << 16, tb[6] | (uint32_t)tb[7] << 16);
-          }
-        }
-      }
-#pragma unroll
-      for (int b = 0; b < 4; b++) {
-        const int i = base + b * QG_THREADS + tid;
-        if (i < items) {
-          const int r = i / noct, o8 = (i - r * noct) * 8;
-          const uint32_t su[4] = {sv[b].x, sv[b].y, sv[b].z, sv[b].w};
-          const uint32_t bu[4] = {bv[b].x, bv[b].y, bv[b].z, bv[b].w};
-          uint32_t* dst = sb + r * g.sbstr + o8;
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            if (o8 + 2 * e < ncg) dst[2 * e] = prmt(su[e], bu[e], 0x5410);
-            if (o8 + 2 * e + 1 < ncg) dst[2 * e + 1] = prmt(su[e], bu[e], 0x7632);
-          }
-        }
-      }
-    }
-  }
+  qg_load_scales(p, g, smem + L.o_sc, cluster_id * rows, KG, cg0, ncg, ntl > 0, tid);
+  qg_load_scales(p, g, smem + L.o_sc + scbuf, (cluster_id + nclusters) * rows, KG, cg0, ncg, ntl > 1, tid);
 
   if (tid < QG_MAXM) smax[tid] = 0u;
   // x may be written by the previous kernel
@@ -383,145 +392,173 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   }
   __syncthreads();
 
-  // ---- stream the warp's groups ----
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};   // scale * sum(x'(code)) - scale * Q, x' domain
-  float accb[4] = {0.f, 0.f, 0.f, 0.f};  // bias * X
+#ifdef QG_X_TRACE
+  if (lane == 0) atomicAdd(&qg_trace[6], globaltimer() - t_start);
+#endif
+  // ---- stream the warp's stages, tile after tile ----
   const bool tv = gq < M;
   const uint8_t* xlane = xs + (size_t)(tv ? gq : 0) * g.xstr + (size_t)c * (GS / 4) * 2;
-  const uint32_t* sb0p = sb + (s * 16 + gq) * g.sbstr;
-  const uint32_t* sb1p = sb0p + 8 * g.sbstr;
+  int off0[GC][NH], off1[GC][NH];  // lane-constant swizzled offsets of rows gq, gq + 8
+#pragma unroll
+  for (int gi = 0; gi < GC; gi++)
+#pragma unroll
+    for (int h = 0; h < NH; h++) {
+      off0[gi][h] = swz(gq, gi * GB + c * LB + 16 * h);
+      off1[gi][h] = swz(gq + 8, gi * GB + c * LB + 16 * h);
+    }
+  const float e0 = 2 * c < M ? xscale[2 * c] : 0.f, e1 = 2 * c + 1 < M ? xscale[2 * c + 1] : 0.f;
   bool ok = true;
-  for (int j = 0; j < nch; j++) {
-    const int st = j % D;
-    ok &= mbar_wait(&bars[st], (uint32_t)(j / D) & 1u);
-    const uint8_t* stg = ring + st * QG_STAGE_BYTES;
-#pragma unroll
-    for (int gi = 0; gi < GC; gi++) {
-      if (j * GC + gi < nwg) {
-        const int gl = wg0 + j * GC + gi;
-        uint32_t w0[WL], w1[WL];
-        lds_lane<LB>(stg, gq, gi * GB + c * LB, w0);
-        lds_lane<LB>(stg, gq + 8, gi * GB + c * LB, w1);
-        float ag[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint8_t* xp = xlane + (size_t)gl * GS * 2;
-#if defined(QG_X_NOMMA)
-        ag[0] = __uint_as_float(w0[0] ^ w1[WL - 1]); ag[1] = ag[0]; ag[2] = ag[0]; ag[3] = ag[0];
-        if (false) {
-#else
-        if constexpr (BITS == 4) {
-#endif
-#pragma unroll
-          for (int wi = 0; wi < WL; wi++) {
-            uint32_t pa[4], pb[4];
-            unpack4h(w0[wi], pa);
-            unpack4h(w1[wi], pb);
-            uint4 xv = make_uint4(0, 0, 0, 0);
-            if (tv) xv = *reinterpret_cast<const uint4*>(xp + wi * 16);
-            const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]};
-            const uint32_t a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-            mma_f16_16816(ag, a0, xv.x, xv.y);
-            mma_f16_16816(ag, a1, xv.z, xv.w);
-          }
-        } else {
-#pragma unroll
-          for (int wi = 0; wi < WL; wi++) {
-            uint32_t pa[2], pb[2];
-            unpack8h(w0[wi], pa);
-            unpack8h(w1[wi], pb);
-            uint2 xv = make_uint2(0, 0);
-            if (tv) xv = *reinterpret_cast<const uint2*>(xp + wi * 8);
-            const uint32_t a[4] = {pa[0], pb[0], pa[1], pb[1]};
-            mma_f16_16816(ag, a, xv.x, xv.y);
-          }
-        }
-#if defined(QG_X_NOFOLD)
-        acc[0] += ag[0]; acc[1] += ag[1]; acc[2] += ag[2]; acc[3] += ag[3];
-        if (false) {
-#else
-        {
-#endif
-        const uint32_t q0 = sb0p[gl], q1 = sb1p[gl];
-        const float s0 = __uint_as_float(q0 << 16), s1 = __uint_as_float(q1 << 16);
-        const float b0 = __uint_as_float(q0 & 0xFFFF0000u), b1 = __uint_as_float(q1 & 0xFFFF0000u);
-        const float2 xq = *reinterpret_cast<const float2*>(xsumq + gl * QG_TOKP + 2 * c);
-        const float2 xb = *reinterpret_cast<const float2*>(xsumb + gl * QG_TOKP + 2 * c);
-        acc[0] = fmaf(s0, ag[0] - xq.x, acc[0]);
-        acc[1] = fmaf(s0, ag[1] - xq.y, acc[1]);
-        acc[2] = fmaf(s1, ag[2] - xq.x, acc[2]);
-        acc[3] = fmaf(s1, ag[3] - xq.y, acc[3]);
-        accb[0] = fmaf(b0, xb.x, accb[0]);
-        accb[1] = fmaf(b0, xb.y, accb[1]);
-        accb[2] = fmaf(b1, xb.x, accb[2]);
-        accb[3] = fmaf(b1, xb.y, accb[3]);
-        }
-      }
-    }
-    // refill this stage once every lane has read it (generic reads before the async write)
-    __syncwarp();
-    if (lane == 0 && j + D < nch) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive_expect_tx(&bars[st], QG_STAGE_BYTES);
-      tma_load_2d(ring + st * QG_STAGE_BYTES, &tmw, wx0 + (j + D) * GC * GB, wrow, &bars[st]);
-    }
-  }
-  if (!ok && p.status) atomicExch(p.status, VMLX_E_STATE);
+  int j = 0, st = 0;
+  uint32_t phase = 0;
+  for (int64_t ti = 0; ti < ntl; ti++) {
+    const int64_t row0 = (cluster_id + ti * nclusters) * rows;
+    uint8_t* scb = smem + L.o_sc + (size_t)(ti & 1) * scbuf;
+    cp_async_wait1();  // this tile's scales (all but the newest copy group)
+    __syncthreads();   // ... visible to every thread; the previous tile's reduction is done
+    const bf16* sc0 = reinterpret_cast<const bf16*>(scb + (size_t)(s * 16 + gq) * g.sbrow);
+    const bf16* sc1 = reinterpret_cast<const bf16*>(scb + (size_t)(s * 16 + gq + 8) * g.sbrow);
+    const bf16* bi0 = reinterpret_cast<const bf16*>(scb + (size_t)(rows + s * 16 + gq) * g.sbrow);
+    const bf16* bi1 = reinterpret_cast<const bf16*>(scb + (size_t)(rows + s * 16 + gq + 8) * g.sbrow);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};   // scale * (sum(x' code) - Q), x' domain
+    float accb[4] = {0.f, 0.f, 0.f, 0.f};  // bias * X
+    for (int jj = 0; jj < nch; jj++, j++) {  // j: this warp's stage counter
 
-  // ---- fixed-order reduction: warps of the CTA, then the CTAs of the cluster ----
-  // accumulator (row gq / gq+8, tokens 2c, 2c+1) -> red[warp][row][token]
-  {
-    // back from the x' domain: y = 2^-s * acc + accb
-    const float e0 = 2 * c < M ? xscale[2 * c] : 0.f, e1 = 2 * c + 1 < M ? xscale[2 * c + 1] : 0.f;
-    float* rw = red + (size_t)warp * 16 * QG_TOKP;
-    *reinterpret_cast<float2*>(rw + gq * QG_TOKP + 2 * c) =
-        make_float2(fmaf(acc[0], e0, accb[0]), fmaf(acc[1], e1, accb[1]));
-    *reinterpret_cast<float2*>(rw + (gq + 8) * QG_TOKP + 2 * c) =
-        make_float2(fmaf(acc[2], e0, accb[2]), fmaf(acc[3], e1, accb[3]));
-  }
-  __syncthreads();
-  const int KSPLIT = QG_WARPS / S;
-  for (int i = tid; i < 16 * S * M; i += QG_THREADS) {
-    const int r = i / M, t = i - r * M;
-    const int ss_ = r >> 4, rr = r & 15;
-    float v = 0.f;
-    for (int q = 0; q < KSPLIT; q++) v += red[((size_t)(q * S + ss_) * 16 + rr) * QG_TOKP + t];
-    if (C == 1) {
-      const int64_t n = row_base + r;
-      if (n < p.N) {
-        const int64_t idx = (int64_t)t * p.N + n;
-        if (p.residual) {
-          const float sv = __bfloat162float(__float2bfloat16_rn(v));
-          p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
-        } else {
-          p.y[idx] = __float2bfloat16_rn(v);
+#ifdef QG_X_TRACE
+      const uint64_t t_a = globaltimer();
+#endif
+      ok &= mbar_wait(&bars[st], phase);
+#ifdef QG_X_TRACE
+      const uint64_t t_b = globaltimer();
+      if (lane == 0) { atomicAdd(&qg_trace[0], t_b - t_a); atomicAdd(&qg_trace[1], 1ull); }
+#endif
+      const uint8_t* stg = ring + st * QG_STAGE_BYTES;
+#pragma unroll
+      for (int gi = 0; gi < GC; gi++) {
+        if (jj * GC + gi < nwg) {
+          const int gl = wg0 + jj * GC + gi;
+          uint32_t w0[WL], w1[WL];
+#pragma unroll
+          for (int h = 0; h < NH; h++) {
+            lds_lane<LBH>(stg + off0[gi][h], *reinterpret_cast<uint32_t(*)[LBH / 4]>(w0 + h * 4));
+            lds_lane<LBH>(stg + off1[gi][h], *reinterpret_cast<uint32_t(*)[LBH / 4]>(w1 + h * 4));
+          }
+          float ag[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint8_t* xp = xlane + (size_t)gl * GS * 2;
+          if constexpr (BITS == 4) {
+#pragma unroll
+            for (int wi = 0; wi < WL; wi++) {
+              uint32_t pa[4], pb[4];
+              unpack4h(w0[wi], pa);
+              unpack4h(w1[wi], pb);
+              uint4 xv = make_uint4(0, 0, 0, 0);
+              if (tv) xv = *reinterpret_cast<const uint4*>(xp + wi * 16);
+              const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]};
+              const uint32_t a1[4] = {pa[2], pb[2], pa[3], pb[3]};
+              mma_f16_16816(ag, a0, xv.x, xv.y);
+              mma_f16_16816(ag, a1, xv.z, xv.w);
+            }
+          } else {
+#pragma unroll
+            for (int wi = 0; wi < WL; wi++) {
+              uint32_t pa[2], pb[2];
+              unpack8h(w0[wi], pa);
+              unpack8h(w1[wi], pb);
+              uint2 xv = make_uint2(0, 0);
+              if (tv) xv = *reinterpret_cast<const uint2*>(xp + wi * 8);
+              const uint32_t a[4] = {pa[0], pb[0], pa[1], pb[1]};
+              mma_f16_16816(ag, a, xv.x, xv.y);
+            }
+          }
+          const float s0 = __bfloat162float(sc0[gl]), s1 = __bfloat162float(sc1[gl]);
+          const float b0 = __bfloat162float(bi0[gl]), b1 = __bfloat162float(bi1[gl]);
+          const float2 xq = *reinterpret_cast<const float2*>(xsumq + gl * QG_TOKP + 2 * c);
+          const float2 xb = *reinterpret_cast<const float2*>(xsumb + gl * QG_TOKP + 2 * c);
+          acc[0] = fmaf(s0, ag[0] - xq.x, acc[0]);
+          acc[1] = fmaf(s0, ag[1] - xq.y, acc[1]);
+          acc[2] = fmaf(s1, ag[2] - xq.x, acc[2]);
+          acc[3] = fmaf(s1, ag[3] - xq.y, acc[3]);
+          accb[0] = fmaf(b0, xb.x, accb[0]);
+          accb[1] = fmaf(b0, xb.y, accb[1]);
+          accb[2] = fmaf(b1, xb.x, accb[2]);
+          accb[3] = fmaf(b1, xb.y, accb[3]);
         }
       }
-    } else {
-      ctile[r * QG_TOKP + t] = v;
+      // refill this stage once every lane has read it (generic reads before the async write)
+      __syncwarp();
+      if (lane == 0 && j + QG_STAGES < total_st) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(st);
+      }
+      if (++st == QG_STAGES) {
+        st = 0;
+        phase ^= 1u;
+      }
     }
-  }
-  if (C > 1) {
-    cluster_arrive();
-    cluster_wait();
-    cg::cluster_group cluster = cg::this_cluster();
-    const int rlo = crank * 16 * S / C, rhi = (crank + 1) * 16 * S / C;
-    for (int i = tid; i < (rhi - rlo) * M; i += QG_THREADS) {
-      const int r = rlo + i / M, t = i % M;
+
+    // ---- fixed-order reduction: warps of the CTA, then the CTAs of the cluster ----
+    // back from the x' domain (y = 2^-s acc + accb): (row gq / gq+8, tokens 2c, 2c+1)
+    {
+      float* rw = red + (size_t)warp * 16 * QG_TOKP;
+      *reinterpret_cast<float2*>(rw + gq * QG_TOKP + 2 * c) =
+          make_float2(fmaf(acc[0], e0, accb[0]), fmaf(acc[1], e1, accb[1]));
+      *reinterpret_cast<float2*>(rw + (gq + 8) * QG_TOKP + 2 * c) =
+          make_float2(fmaf(acc[2], e0, accb[2]), fmaf(acc[3], e1, accb[3]));
+    }
+    __syncthreads();
+    // the buffer of this tile's scales is free: start copying the scales two tiles ahead
+    qg_load_scales(p, g, scb, (cluster_id + (ti + 2) * nclusters) * rows, KG, cg0, ncg, ti + 2 < ntl, tid);
+    const int KSPLIT = QG_WARPS / S;
+    for (int i = tid; i < rows * M; i += QG_THREADS) {
+      const int r = i / M, t = i - r * M;
+      const int ss_ = r >> 4, rr = r & 15;
       float v = 0.f;
-      for (int q = 0; q < C; q++) v += cluster.map_shared_rank(ctile, q)[r * QG_TOKP + t];
-      const int64_t n = row_base + r;
-      if (n < p.N) {
-        const int64_t idx = (int64_t)t * p.N + n;
-        if (p.residual) {
-          const float sv = __bfloat162float(__float2bfloat16_rn(v));
-          p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
-        } else {
-          p.y[idx] = __float2bfloat16_rn(v);
+      for (int q = 0; q < KSPLIT; q++) v += red[((size_t)(q * S + ss_) * 16 + rr) * QG_TOKP + t];
+      if (C == 1) {
+        const int64_t n = row0 + r;
+        if (n < p.N) {
+          const int64_t idx = (int64_t)t * p.N + n;
+          if (p.residual) {
+            const float sv = __bfloat162float(__float2bfloat16_rn(v));
+            p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
+          } else {
+            p.y[idx] = __float2bfloat16_rn(v);
+          }
         }
+      } else {
+        ctile[r * QG_TOKP + t] = v;
       }
     }
-    cluster_arrive();  // keep this CTA's shared memory alive until every peer has read it
-    cluster_wait();
+    if (C > 1) {
+      cluster_arrive();
+      cluster_wait();
+      cg::cluster_group cluster = cg::this_cluster();
+      const int rlo = crank * rows / C, rhi = (crank + 1) * rows / C;
+      for (int i = tid; i < (rhi - rlo) * M; i += QG_THREADS) {
+        const int r = rlo + i / M, t = i % M;
+        float v = 0.f;
+        for (int q = 0; q < C; q++) v += cluster.map_shared_rank(ctile, q)[r * QG_TOKP + t];
+        const int64_t n = row0 + r;
+        if (n < p.N) {
+          const int64_t idx = (int64_t)t * p.N + n;
+          if (p.residual) {
+            const float sv = __bfloat162float(__float2bfloat16_rn(v));
+            p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
+          } else {
+            p.y[idx] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+      cluster_arrive();  // peers have read this CTA's tile before it is overwritten or freed
+      cluster_wait();
+    }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+#ifdef QG_X_TRACE
+  if (lane == 0) { atomicAdd(&qg_trace[2], globaltimer() - t_start); atomicAdd(&qg_trace[3], 1ull); }
+  if (tid == 0) atomicMax(&qg_trace[4], globaltimer());
+  if (tid == 0) atomicMin(&qg_trace[5], t_start);
+#endif
+  if (!ok && p.status) atomicExch(p.status, VMLX_E_STATE);
 }
 
 // ---- host side -------------------------------------------------------------
@@ -531,44 +568,55 @@ static int env_int(const char* name, int dflt) {
   return v && *v ? atoi(v) : dflt;
 }
 
-// Geometry from (N, K, bits, group size) only.  Cost, in units of one warp streaming one
-// 16-row group: the busiest SM's share of whole CTAs, plus a fixed cost per CTA wave
-// (prologue, DRAM latency) and per cluster reduction.  Shared memory is sized for the
-// largest M of the regime so that the geometry never depends on M.
+static int qg_per_sm(const QgSmem& L) {
+  int per = (int)((228 * 1024) / (L.total + 1024));
+  return per > 3 ? 3 : per;  // 80 registers x 256 threads: 3 CTAs per SM
+}
+
+static void qg_fill(QgGeom& gm, int64_t N, int64_t K, int gs, int S, int C) {
+  const int64_t KG = K / gs;
+  gm.S = S;
+  gm.C = C;
+  int KGC = (int)((KG + C - 1) / C);
+  KGC = (KGC + 7) / 8 * 8;  // whole 16-byte scale chunks per CTA
+  gm.KGC = KGC;
+  gm.xstr = KGC * gs * 2 + 16;
+  gm.sbrow = KGC * 2 + 16;
+  gm.ntiles = (int)((N + 16 * S - 1) / (16 * S));
+}
+
+// Geometry from (N, K, bits, group size) only.  The busiest CTA's work (tiles x ring
+// stages per warp, plus a fixed cost per tile and per cluster reduction) against the
+// bandwidth share of the resident CTAs; shared memory is sized for the regime's largest
+// M so that the geometry never depends on M.
 static bool qg_choose(int64_t N, int64_t K, int bits, int gs, QgGeom& best) {
   const int64_t KG = K / gs;
-  const int64_t strips = (N + 15) / 16;
+  const int GC = 128 / (gs * bits / 8);
   const int sms = sm_count();
+  const int forceS = env_int("VMLX_QG_S", 0), forceC = env_int("VMLX_QG_C", 0);
   double best_cost = 1e30;
   bool found = false;
-  const int forceS = env_int("VMLX_QG_S", 0), forceC = env_int("VMLX_QG_C", 0);
-  for (int C = 1; C <= QG_MAX_CLUSTER && C <= KG; C++) {
+  for (int C = 1; C <= QG_MAX_CLUSTER; C++) {
     if (forceC && C != forceC) continue;
-    const int KGC = (int)((KG + C - 1) / C);
-    if ((int64_t)(C - 1) * KGC >= KG) continue;  // an empty CTA
+    if (C > 1 && (int64_t)(C - 1) * (((KG + C - 1) / C + 7) / 8 * 8) >= KG) continue;  // an empty CTA
     for (int S = 1; S <= QG_WARPS; S *= 2) {
       if (forceS && S != forceS) continue;
-      const int KSPLIT = QG_WARPS / S;
       QgGeom gm;
-      gm.S = S;
-      gm.C = C;
-      gm.KGC = KGC;
-      const int GC = 128 / (gs * bits / 8);
-      gm.GW = ((KGC + KSPLIT - 1) / KSPLIT + GC - 1) / GC * GC;  // whole ring stages per warp
-      if ((int64_t)(KSPLIT - 1) * gm.GW >= KGC && KSPLIT > 1) continue;  // an idle warp
-      gm.xstr = KGC * gs * 2 + 16;
-      gm.sbstr = (KGC + 7) / 8 * 8 + 1;
-      gm.D = env_int("VMLX_QG_D", QG_STAGES);
-      gm.dbg = env_int("VMLX_QG_DBG", 0);
+      qg_fill(gm, N, K, gs, S, C);
+      const int KSPLIT = QG_WARPS / S;
+      gm.GW = ((gm.KGC + KSPLIT - 1) / KSPLIT + GC - 1) / GC * GC;
+      if (KSPLIT > 1 && (int64_t)(KSPLIT - 1) * gm.GW >= gm.KGC && !forceS) continue;  // an idle warp
       QgSmem L;
       L.init(gm, QG_MAXM);
       if (L.total > 200 * 1024) continue;
-      const int64_t ctas = (strips + S - 1) / S * C;
-      const int per_sm = (int)((220 * 1024) / (L.total + 2048)) < 3 ? (int)((220 * 1024) / (L.total + 2048)) : 3;
+      const int per_sm = qg_per_sm(L);
       if (per_sm < 1) continue;
-      const double waves = (double)((ctas + (int64_t)sms * per_sm - 1) / ((int64_t)sms * per_sm));
-      const double stream = (double)((ctas + sms - 1) / sms) * QG_WARPS * gm.GW;
-      const double cost = stream + 120.0 * waves + (C > 1 ? 80.0 : 0.0) + 0.01 * S;
+      const int64_t nclu = std::min<int64_t>(gm.ntiles, (int64_t)sms * per_sm / C);
+      if (nclu < 1) continue;
+      const int64_t tiles_per = (gm.ntiles + nclu - 1) / nclu;
+      const double stages = (double)tiles_per * (gm.GW / GC);           // per warp, serial
+      const double bw = (double)(N / 16) * KG / GC / ((double)sms * 24);  // stages per warp slot if BW-bound
+      const double cost = std::max(stages, bw) + 1.5 * tiles_per + (C > 1 ? 2.0 * tiles_per : 0.0);
       if (cost < best_cost) {
         best_cost = cost;
         best = gm;
@@ -585,7 +633,7 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
   if (!qg_choose(a.N, a.K, BITS, GS, g))
     return set_error(VMLX_E_UNSUPPORTED, "qgemv: no launch geometry for N=%lld K=%lld", (long long)a.N,
                      (long long)a.K);
-  g.sc_vec = (a.K / GS) % 8 == 0 && g.KGC % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
+  g.sc_async = (a.K / GS) % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
   QgSmem L;
   L.init(g, (int)a.M);
   auto kern = qgemv_kernel<BITS, GS>;
@@ -593,10 +641,11 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
     const int rc = ensure_max_dynamic_smem((const void*)kern, 220 * 1024);
     if (rc) return rc;
   }
-  const int64_t ctas = (a.N + 16 * g.S - 1) / (16 * g.S) * g.C;
-  if (ctas >= (1LL << 31)) return set_error(VMLX_E_UNSUPPORTED, "qgemv: N=%lld too large", (long long)a.N);
+  QgSmem Lmax;
+  Lmax.init(g, QG_MAXM);
+  const int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(Lmax) / g.C);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+  cfg.gridDim = dim3((unsigned)(nclu * g.C), 1, 1);
   cfg.blockDim = dim3(QG_THREADS);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
@@ -625,7 +674,7 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
 bool qgemv_covers(const QmvArgs& a, int mode, int bits, int gs) {
   if (mode != QMV_DENSE || a.tp_world > 1) return false;
   if (a.M < 1 || a.M > QG_MAXM) return false;
-  if (a.K % 8) return false;
+  if (a.K % 8 || a.N >= (1LL << 31)) return false;
   if (!aligned(a.x, 16) || (a.norm_w && !aligned(a.norm_w, 16))) return false;
   if (!env_int("VMLX_QG", 0) || env_int("VMLX_QG_DISABLE", 0)) return false;
   (void)bits;

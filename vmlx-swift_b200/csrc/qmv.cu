@@ -166,7 +166,7 @@ __device__ __forceinline__ QmvItem qmv_item(const QmvArgs& p, int mode, int64_t 
   it.zero_rows = false;
   if (mode == QMV_GATHER) {
     it.base = z;
-    it.e = (int64_t)p.rhs[z];
+    it.e = p.rhs ? (int64_t)p.rhs[z] : z * p.n_experts / p.batch;
     if (it.e >= p.n_experts) { it.zero_rows = true; it.e = 0; }
   } else if (mode == QMV_SORTED) {
     it.e = z;
@@ -256,6 +256,10 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
 
   if (warp == QMV_CWARPS) {
     // ======================= producer warp (lane 0 issues) =======================
+    // In the gathered modes the work items depend on the expert indices, which the
+    // previous kernel may still be writing: wait for it before the first item (the
+    // dense mode streams static weights ahead of the wait).
+    if (mode != QMV_DENSE) asm volatile("griddepcontrol.wait;" ::: "memory");
     bool pend = false;
     for (int64_t item = it_lo; item < it_hi; item += it_step) {
       const QmvItem I = qmv_item(p, mode, item, rowtiles);

@@ -66,16 +66,22 @@ __host__ __device__ inline size_t tp_epoch_off(size_t max_bytes, int world) {
 // Region of the fused row-parallel GEMV + all-reduce (its own slots, so that its
 // parity never aliases the standalone all_sum's): [2][world][max_bytes] slots,
 // [2][world][TP_FUSED_MAXC] flags, then {epoch, finished-CTA counter}.
-inline size_t tp_fused_slots_off(size_t max_bytes, int world) {
+__host__ __device__ inline size_t tp_fused_slots_off(size_t max_bytes, int world) {
   return (tp_epoch_off(max_bytes, world) + TP_MAX_CTAS * sizeof(uint32_t) + 255) / 256 * 256;
 }
-inline size_t tp_fused_flags_off(size_t max_bytes, int world) {
+__host__ __device__ inline size_t tp_fused_flags_off(size_t max_bytes, int world) {
   return tp_fused_slots_off(max_bytes, world) + (size_t)2 * world * max_bytes;
 }
-inline size_t tp_fused_epoch_off(size_t max_bytes, int world) {
+__host__ __device__ inline size_t tp_fused_epoch_off(size_t max_bytes, int world) {
   return tp_fused_flags_off(max_bytes, world) + (size_t)2 * world * TP_FUSED_MAXC * sizeof(uint32_t);
 }
-inline size_t tp_total_bytes(size_t max_bytes, int world) { return tp_fused_epoch_off(max_bytes, world) + 256; }
+// Slots of the standalone low-latency all_sum ([2][world][max_bytes] of 8-byte {value,
+// epoch} words), apart from the flag protocol's slots: a stale word of packed bf16 data
+// left there by a flag-protocol call could otherwise carry a matching "epoch".
+__host__ __device__ inline size_t tp_ll_slot_off(int parity, int src, size_t max_bytes, int world) {
+  return ((tp_fused_epoch_off(max_bytes, world) + 256 + 255) / 256 * 256) + ((size_t)parity * world + src) * max_bytes;
+}
+inline size_t tp_total_bytes(size_t max_bytes, int world) { return tp_ll_slot_off(2, 0, max_bytes, world); }
 
 // Every all_sum call (either protocol) has one epoch for all its CTAs: read from
 // epoch[0] at the start, written back by the grid's last CTA (epoch[1] counts finished
@@ -153,8 +159,9 @@ tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf
 
 // Low-latency all-reduce for small vectors (n * 8 <= max_bytes): every element travels as
 // one 8-byte word {bf16 bits, epoch} (single system-scope store), and readers poll the
-// words themselves, so there is no fence and no flag round trip.  Same slots, parities
-// and per-CTA epochs as the flag protocol above; same rank-order fp32 sum.
+// words themselves, so there is no fence and no flag round trip.  Its own slot region
+// (tp_ll_slot_off), the same parities and per-call epochs as the flag protocol above;
+// same rank-order fp32 sum.
 __global__ void __launch_bounds__(TP_THREADS)
 tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
                      bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns) {
@@ -169,12 +176,12 @@ tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const
   const uint32_t e = s_epoch;
   const int parity = e & 1;
   for (int r = 0; r < world; r++) {
-    uint64_t* dst = reinterpret_cast<uint64_t*>(peers.buf[r] + tp_slot_off(parity, rank, max_bytes, world));
+    uint64_t* dst = reinterpret_cast<uint64_t*>(peers.buf[r] + tp_ll_slot_off(parity, rank, max_bytes, world));
     for (int64_t i = e0 + threadIdx.x; i < e1; i += TP_THREADS)
       st_ll(dst + i, (uint32_t)__bfloat16_as_ushort(in[i]), e);
   }
   const uint64_t deadline = globaltimer() + timeout_ns;
-  const uint64_t* slots = reinterpret_cast<const uint64_t*>(mine + tp_slot_off(parity, 0, max_bytes, world));
+  const uint64_t* slots = reinterpret_cast<const uint64_t*>(mine + tp_ll_slot_off(parity, 0, max_bytes, world));
   const size_t rstride = max_bytes / sizeof(uint64_t);
   bool ok = true;
   for (int64_t i = e0 + threadIdx.x; i < e1 && ok; i += TP_THREADS) {

@@ -169,3 +169,49 @@ class QuantizedShardedToAllLinear:
             out.copy_(y)
             y = out
         return y
+
+
+def group_split(n_groups: int, world: int, rank: int):
+    """Whole quantization groups [g0, g1) of rank `rank` when n_groups do not divide evenly:
+    the first n_groups % world ranks take one extra group (12 groups over 8 ranks:
+    2,2,2,2,1,1,1,1).  Slicing at group boundaries keeps every shard a bit-exact slice of
+    the quantized tensors (nothing is re-quantized)."""
+    base, extra = divmod(n_groups, world)
+    g0 = rank * base + min(rank, extra)
+    return g0, g0 + base + (1 if rank < extra else 0)
+
+
+class ShardedSwitchGLU:
+    """SwitchGLU with the expert intermediate dimension sharded over a TP group (BASELINE
+    config 4: Qwen3-30B-A3B's 128 experts, FFN 768, over TP=1/2/4/8).  Each rank keeps
+    gate/up rows and down columns [g0*gs, g1*gs) of every expert (group_split, uneven when
+    F/gs does not divide), runs the whole routed SwitchGLU + weighted combine on its slice
+    (a partial sum of the block output) and all-reduces the [T, H] result once.
+
+    The reference replicates experts under TP (Libraries/MLXDistributedTP/
+    ShardingPlans+Qwen35.swift:14-19); sharding the intermediate is the TP layout of the
+    MoE down projection as a row-parallel linear (LinearLayers.swift:161-205)."""
+
+    def __init__(self, glu, group: Group):
+        from .switch_layers import QuantizedSwitchLinear, SwitchGLU
+        gp, up, dn = glu.gate_proj, glu.up_proj, glu.down_proj
+        gs, bits = dn.group_size, dn.bits
+        F = gp.output_dims
+        if F % gs:
+            raise VMLXError(_lib.VMLX_E_INVALID, f"intermediate {F} is not a whole number of {gs}-groups")
+        g0, g1 = group_split(F // gs, group.size, group.rank)
+        r0, r1 = g0 * gs, g1 * gs
+        w0, w1 = r0 * bits // 32, r1 * bits // 32
+
+        def rows(sl):  # column-parallel over the intermediate (output rows of gate / up)
+            return QuantizedSwitchLinear(sl.weight[:, r0:r1].contiguous(), sl.scales[:, r0:r1].contiguous(),
+                                         sl.biases[:, r0:r1].contiguous(), None, gs, bits, sl.mode)
+        down = QuantizedSwitchLinear(dn.weight[..., w0:w1].contiguous(), dn.scales[..., g0:g1].contiguous(),
+                                     dn.biases[..., g0:g1].contiguous(), None, gs, bits, dn.mode)
+        self.local = SwitchGLU(rows(gp), rows(up), down)
+        self.group, self.groups = group, (g0, g1)
+
+    def combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        """sum_j SwitchGLU(x, indices)[:, j] * scores[:, j], reduced over the group."""
+        y = self.local.combined(x, indices, scores)
+        return self.group.all_sum(y)

@@ -199,3 +199,51 @@ def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
         lhs32.data_ptr() if lhs32 is not None else None, rhs32.data_ptr(), transpose, group_size,
         bits, mode.encode() if mode else None, sorted_indices, nb, x_batches, M, N, K, E, _stream(x)))
     return y
+
+
+# ---- MoE routing (Libraries/MLXLLM/Models/Qwen3MoE.swift:137-152,
+#      Libraries/MLXLMCommon/SwitchLayers.swift:64-83) ---------------------------------
+
+def moe_route(logits: torch.Tensor, k: int, norm_topk_prob: bool = False):
+    """softmax(logits, precise) -> (indices uint32-valued int32 [.., k], scores [.., k] in
+    the logits' dtype): the k experts with the largest logits (descending), their
+    softmax probabilities, optionally renormalised to sum to one."""
+    _need_cuda(logits)
+    lg = logits.contiguous()
+    E = lg.shape[-1]
+    rows = lg.numel() // E
+    inds = torch.empty(*lg.shape[:-1], k, dtype=torch.int32, device=lg.device)
+    scores = torch.empty(*lg.shape[:-1], k, dtype=lg.dtype, device=lg.device)
+    check(_lib.lib().vmlx_cuda_moe_route(lg.data_ptr(), _dtype_code(lg.dtype), rows, E, k, norm_topk_prob,
+                                         inds.data_ptr(), scores.data_ptr(), _stream(lg)))
+    return inds, scores
+
+
+def moe_sort(indices: torch.Tensor, n_experts: int):
+    """gatherSort on the device: (sorted expert ids, token row of each sorted pair,
+    inverse order), all int32 [tokens * k]; a stable sort of the flattened indices."""
+    _need_cuda(indices)
+    k = indices.shape[-1]
+    flat = indices.reshape(-1).to(torch.int32).contiguous()
+    P = flat.numel()
+    sorted_ids = torch.empty(P, dtype=torch.int32, device=flat.device)
+    lhs = torch.empty_like(sorted_ids)
+    inv = torch.empty_like(sorted_ids)
+    check(_lib.lib().vmlx_cuda_moe_sort(flat.data_ptr(), P, k, n_experts, sorted_ids.data_ptr(), lhs.data_ptr(),
+                                        inv.data_ptr(), None, _stream(flat)))
+    return sorted_ids, lhs, inv
+
+
+def moe_combine(y: torch.Tensor, scores: torch.Tensor, inverse_order: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[t] = sum_j y[src(t, j)] * scores[t, j] (bf16 out); y [tokens * k, D] in sorted
+    order when inverse_order is given (scatterUnsort folded in), else [tokens, k, D]."""
+    _need_cuda(y, scores)
+    T, k = scores.shape[0], scores.shape[-1]
+    D = y.shape[-1]
+    yc = y.reshape(-1, D).contiguous()
+    sc = scores.reshape(T, k).contiguous()
+    out = torch.empty(T, D, dtype=torch.bfloat16, device=y.device)
+    inv = inverse_order.to(torch.int32).contiguous() if inverse_order is not None else None
+    check(_lib.lib().vmlx_cuda_moe_combine(yc.data_ptr(), inv.data_ptr() if inv is not None else None, sc.data_ptr(),
+                                           _dtype_code(sc.dtype), T, k, D, out.data_ptr(), _stream(yc)))
+    return out

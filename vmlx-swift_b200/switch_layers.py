@@ -1,6 +1,7 @@
 """MoE expert layers (MLXLMCommon/SwitchLayers.swift mirror).
 
-  gather_sort / scatter_unsort   SwitchLayers.swift:64-83
+  gather_sort / scatter_unsort   SwitchLayers.swift:64-83 (device sort kernel; x rows by index)
+  Qwen3MoESparseMoeBlock         Qwen3MoE.swift:116-153 (device routing and weighted sum)
   QuantizedSwitchLinear          SwitchLayers.swift:430-512
   SwitchGLU                      SwitchLayers.swift:91-367
     - sort when indices.size >= 64 (:296)
@@ -21,22 +22,23 @@ from . import fast, ops
 FUSED_GATE_UP_THRESHOLD = int(os.environ.get("BENCH_FUSED_GATE_UP_THRESHOLD", str(1 << 30)))
 
 
-def gather_sort(x: torch.Tensor, indices: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Sort the (token, slot) pairs by expert: returns (x rows in sorted order,
-    sorted indices, inverse order).  Stable sort, as MLX's argsort."""
-    m = indices.shape[-1]
-    flat = indices.reshape(-1)
-    order = torch.argsort(flat, stable=True)
-    inv = torch.argsort(order, stable=True)
-    xf = x.reshape(-1, *x.shape[-2:])  # flatten(start: 0, end: -3)
-    return xf[order // m], flat[order], inv
+def gather_sort(x: torch.Tensor, indices: torch.Tensor, n_experts: int):
+    """gatherSort on the device (SwitchLayers.swift:64-75): a stable sort of the
+    (token, slot) pairs by expert.  Returns (x flattened to [rows, 1, D], sorted expert
+    ids, the x row of each sorted pair, inverse order).  The reference gathers
+    x[order / k] into a copy; here the row list goes to gather_qmm as lhs_indices."""
+    sorted_ids, lhs, inv = ops.moe_sort(indices, n_experts)
+    return x.reshape(-1, *x.shape[-2:]), sorted_ids, lhs, inv
 
 
 def scatter_unsort(x: torch.Tensor, inv_order: torch.Tensor, shape=None) -> torch.Tensor:
-    x = x[inv_order]
+    """x[inv_order] (SwitchLayers.swift:77-83) with the combine kernel at weight 1 (exact)."""
+    rows = inv_order.numel()
+    ones = torch.ones(rows, 1, dtype=torch.float32, device=x.device)
+    y = ops.moe_combine(x.reshape(rows, -1), ones, inv_order).reshape(rows, *x.shape[1:])
     if shape is not None:
-        x = x.reshape(*shape, *x.shape[1:])
-    return x
+        y = y.reshape(*shape, *y.shape[1:])
+    return y
 
 
 class QuantizedSwitchLinear:
@@ -63,8 +65,8 @@ class QuantizedSwitchLinear:
     def input_dims(self):
         return self.weight.shape[2] * 32 // self.bits
 
-    def __call__(self, x, indices, sorted_indices: bool = False):
-        y = ops.gather_quantized_mm(x, self.weight, self.scales, self.biases, rhs_indices=indices,
+    def __call__(self, x, indices, sorted_indices: bool = False, lhs: Optional[torch.Tensor] = None):
+        y = ops.gather_quantized_mm(x, self.weight, self.scales, self.biases, lhs_indices=lhs, rhs_indices=indices,
                                     transpose=True, group_size=self.group_size, bits=self.bits,
                                     mode=self.mode, sorted_indices=sorted_indices)
         if self.bias is not None:
@@ -88,22 +90,54 @@ class SwitchGLU:
                     torch.cat([g.biases, u.biases], 1), None, g.group_size, g.bits, g.mode)
         return self._fused
 
-    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    def _expert_outputs(self, x: torch.Tensor, indices: torch.Tensor):
+        """Per-pair down outputs, in sorted order when the pairs were sorted.
+        Returns (y [pairs, 1, D], inverse order or None)."""
         fused = self.ensure_fused_gate_up()
         use_fused = fused is not None and indices.numel() <= FUSED_GATE_UP_THRESHOLD
         x = x.unsqueeze(-2).unsqueeze(-3)  # expandedDimensions(x, [-2, -3])
         do_sort = indices.numel() >= 64
-        idx, inv = indices, None
+        idx, inv, lhs = indices, None, None
         if do_sort:
-            x, idx, inv = gather_sort(x, indices)
+            x, idx, lhs, inv = gather_sort(x, indices, self.down_proj.num_experts)
         if use_fused:
-            comb = fused(x, idx, sorted_indices=do_sort)
+            comb = fused(x, idx, sorted_indices=do_sort, lhs=lhs)
             act = fast.silu_mul(comb)  # silu(gate) * up in one kernel over the gate||up rows
         else:
-            up = self.up_proj(x, idx, sorted_indices=do_sort)
-            gate = self.gate_proj(x, idx, sorted_indices=do_sort)
+            up = self.up_proj(x, idx, sorted_indices=do_sort, lhs=lhs)
+            gate = self.gate_proj(x, idx, sorted_indices=do_sort, lhs=lhs)
             act = fast.silu_mul(torch.cat([gate, up], -1))
         y = self.down_proj(act.contiguous(), idx, sorted_indices=do_sort)
-        if do_sort:
+        return y, inv
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        y, inv = self._expert_outputs(x, indices)
+        if inv is not None:
             y = scatter_unsort(y, inv, indices.shape)
+        else:
+            y = y.reshape(*indices.shape, *y.shape[-2:])
         return y.squeeze(-2)
+
+    def combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        """sum_j SwitchGLU(x, indices)[:, j] * scores[:, j] with the unsort folded into the
+        weighted sum (one kernel): the MoE block's output (Qwen3MoE.swift:150-151)."""
+        y, inv = self._expert_outputs(x, indices)
+        T = indices.reshape(-1, indices.shape[-1]).shape[0]
+        return ops.moe_combine(y.reshape(-1, y.shape[-1]), scores.reshape(T, -1), inv)
+
+
+class Qwen3MoESparseMoeBlock:
+    """Qwen3MoESparseMoeBlock (Libraries/MLXLLM/Models/Qwen3MoE.swift:116-153): router
+    gate, top-k routing, SwitchGLU, score-weighted sum -- every step a device kernel."""
+
+    def __init__(self, gate, switch_mlp: SwitchGLU, top_k: int, norm_topk_prob: bool = False):
+        self.gate, self.switch_mlp, self.top_k, self.norm_topk_prob = gate, switch_mlp, top_k, norm_topk_prob
+
+    def route(self, logits: torch.Tensor):
+        return ops.moe_route(logits, self.top_k, self.norm_topk_prob)
+
+    def __call__(self, x: torch.Tensor, logits: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if logits is None:
+            logits = self.gate(x)
+        inds, scores = self.route(logits)
+        return self.switch_mlp.combined(x, inds, scores)
