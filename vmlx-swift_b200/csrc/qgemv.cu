@@ -57,8 +57,6 @@ constexpr int QG_STAGE_BYTES = 16 * 128;  // one stage: 16 rows x 128 bytes
 
 template <int BITS, int GS>
 struct QGT {
-  static constexpr int LB = GS * BITS / 32;          // bytes per lane per row per group
-  static constexpr int WL = LB / 4;                  // 32-bit words per lane per row per group
   static constexpr int GB = GS * BITS / 8;           // bytes per row per group
   static constexpr int GC = 128 / GB;                // groups per ring stage
 };
@@ -72,6 +70,7 @@ struct QgGeom {
   int sbrow;     // bytes per staged scale (or bias) row: 16-byte multiple + 16 of padding
   int ntiles;    // row tiles of 16*S rows
   int sc_async;  // scales/biases rows are 16-byte aligned: cp.async them
+  int cpg;       // 16-byte chunks of packed codes per group
 };
 
 struct QgSmem {
@@ -81,7 +80,7 @@ struct QgSmem {
     o_bar = o_ring + (size_t)QG_WARPS * QG_STAGES * QG_STAGE_BYTES;
     o_xs = o_bar + (size_t)QG_WARPS * QG_STAGES * 8;
     o_xsum = o_xs + (size_t)m * g.xstr;
-    o_sc = o_xsum + (size_t)2 * g.KGC * QG_TOKP * 4;
+    o_sc = o_xsum + (size_t)g.KGC * g.cpg * QG_TOKP * 4;
     o_red = o_sc + (size_t)2 * 2 * 16 * g.S * g.sbrow;  // [buffer][scale | bias][row]
     o_ctile = o_red + (size_t)QG_WARPS * 16 * QG_TOKP * 4;
     total = o_ctile + (g.C > 1 ? (size_t)16 * g.S * QG_TOKP * 4 : 0) + 1024;  // + alignment slack
@@ -91,48 +90,6 @@ struct QgSmem {
 // Byte offset of (row r in 0..15, byte o) in a 128-byte-swizzled [16][128] stage:
 // 16-byte chunk j of row r sits at chunk j ^ (r & 7).
 __device__ __forceinline__ int swz(int r, int o) { return r * 128 + ((((o >> 4) ^ (r & 7))) << 4) + (o & 15); }
-
-template <int LB>
-__device__ __forceinline__ void lds_lane(const uint8_t* a, uint32_t (&w)[LB / 4]) {
-  if constexpr (LB == 4) {
-    w[0] = *reinterpret_cast<const uint32_t*>(a);
-  } else if constexpr (LB == 8) {
-    const uint2 v = *reinterpret_cast<const uint2*>(a);
-    w[0] = v.x; w[1] = v.y;
-  } else {
-    const uint4 v = *reinterpret_cast<const uint4*>(a);
-    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-  }
-}
-
-// 4-bit word -> four fp16 pairs, exact: p[0] = (n0, n4) + 1024, p[1] = 16 (n1, n5) + 1024,
-// p[2] = (n2, n6) + 1024, p[3] = 16 (n3, n7) + 1024 (under the fp16 exponent byte 0x64
-// the low 10 bits are an integer mantissa, so a nibble masked at bits 0-3 or 4-7 of a
-// half reads as itself or 16x itself).  One prmt and four lop3 per 8 codes.
-__device__ __forceinline__ void unpack4h(uint32_t w, uint32_t (&p)[4]) {
-  const uint32_t E = 0x64006400u;
-  const uint32_t w2 = prmt(w, 0u, 0x3311);  // bytes (b1, b1, b3, b3)
-  p[0] = (w & 0x000F000Fu) | E;
-  p[1] = (w & 0x00F000F0u) | E;
-  p[2] = (w2 & 0x000F000Fu) | E;
-  p[3] = (w2 & 0x00F000F0u) | E;
-}
-
-// 8-bit word (4 codes) -> (q0, q1) + 1024, (q2, q3) + 1024: the code byte becomes the
-// low mantissa byte under an 0x64 exponent byte.
-__device__ __forceinline__ void unpack8h(uint32_t w, uint32_t (&p)[2]) {
-  p[0] = prmt(w, 0x64646464u, 0x4140);
-  p[1] = prmt(w, 0x64646464u, 0x4342);
-}
-
-// D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
-__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -169,31 +126,21 @@ __device__ __forceinline__ void qg_load_scales(const QmvArgs& p, const QgGeom& g
   cp_async_commit();
 }
 
-#ifdef QG_X_TRACE
-__device__ unsigned long long qg_trace[8];
-extern "C" int vmlx_qg_trace(unsigned long long* out, int reset) {
-  cudaMemcpyFromSymbol(out, qg_trace, sizeof(qg_trace));
-  if (reset) { unsigned long long z[8] = {0, 0, 0, 0, 0, ~0ull, 0, 0}; cudaMemcpyToSymbol(qg_trace, z, sizeof(z)); }
-  return 0;
-}
-#endif
-template <int BITS, int GS>
-__global__ void __launch_bounds__(QG_THREADS, 3)
+template <int GS, int MT>
+__global__ void __launch_bounds__(QG_THREADS, 2)
 qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
+  constexpr int BITS = 4;
   using T = QGT<BITS, GS>;
-  constexpr int LB = T::LB, WL = T::WL, GB = T::GB, GC = T::GC;
+  constexpr int GB = T::GB, GC = T::GC;
   constexpr int BPG = GS / 8;  // 8-value x blocks per group
-  constexpr int NH = (LB + 15) / 16, LBH = LB < 16 ? LB : 16;  // 16-byte pieces of a lane's slice
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   __shared__ float xinv[QG_MAXM];    // fused RMSNorm: 1 / rms per token
-  __shared__ uint32_t smax[QG_MAXM];  // max |x| per token (float bits)
-  __shared__ float xscale[QG_MAXM];   // 2^-s per token
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = lane >> 2, c = lane & 3;
+
   const int S = g.S, C = g.C;
-  const int M = (int)p.M;
+  const int M = MT;
   const int crank = C > 1 ? (int)(blockIdx.x % C) : 0;
   const int64_t cluster_id = blockIdx.x / C, nclusters = gridDim.x / C;
   const int64_t KG = p.K / GS;
@@ -210,8 +157,7 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   QgSmem L;
   L.init(g, M);
   uint8_t* xs = smem + L.o_xs;
-  float* xsumb = reinterpret_cast<float*>(smem + L.o_xsum);  // [g][t] sum of x
-  float* xsumq = xsumb + (size_t)g.KGC * QG_TOKP;              // [g][t] 1024 * sum of staged x
+  float* xsum = reinterpret_cast<float*>(smem + L.o_xsum);  // [chunk][t] sum of the chunk's 32 x
   float* red = reinterpret_cast<float*>(smem + L.o_red);
   float* ctile = reinterpret_cast<float*>(smem + L.o_ctile);
   uint8_t* ring = smem + L.o_ring + (size_t)warp * QG_STAGES * QG_STAGE_BYTES;
@@ -221,9 +167,6 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   // Weights and scales are static: start streaming them before waiting on the
   // previous kernel (programmatic dependent launch), and let the next kernel launch.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-#ifdef QG_X_TRACE
-  const uint64_t t_start = globaltimer();
-#endif
   if (lane == 0) {
     for (int d = 0; d < QG_STAGES; d++) mbar_init(&bars[d], 1);
     fence_mbar_init();
@@ -250,10 +193,8 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   qg_load_scales(p, g, smem + L.o_sc, cluster_id * rows, KG, cg0, ncg, ntl > 0, tid);
   qg_load_scales(p, g, smem + L.o_sc + scbuf, (cluster_id + nclusters) * rows, KG, cg0, ncg, ntl > 1, tid);
 
-  if (tid < QG_MAXM) smax[tid] = 0u;
   // x may be written by the previous kernel
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  __syncthreads();
   if (p.norm_w) {
     // fused RMSNorm: 1 / rms over each token's full row (the order of the other GEMV kernel)
     for (int t = warp; t < M; t += QG_WARPS) {
@@ -275,21 +216,14 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
     }
     __syncthreads();
   }
-  // Stage x in two passes.  Pass 1: load (with the optional SwiGLU / RMSNorm), keep the
-  // bf16 values, the per-group sums X[g][t] (fp32) and each token's max |x| over the
-  // CTA's K range.  Pass 2: scale each token by a power of two 2^s_t (max |x| 2^s_t <
-  // 2^15, exact) into fp16 -- for 4-bit, the positions of odd nibbles get 2^(s_t - 4),
-  // which matches the 16x-scaled codes the unpack produces -- permute to the unpack's
-  // order, and record Q[g][t] = 1024 * sum of the staged values (the codes carry a +1024
-  // offset).  The scale only moves exponents, so results do not depend on it.
+  // Stage x as bf16 (after the optional SwiGLU / RMSNorm) and the sum of every 32-value
+  // chunk (one 16-byte chunk of packed 4-bit codes) per token, in fp32.
   {
-    const int nkb = ncg * BPG;
+    const int nkb = ncg * BPG;  // 8-value blocks per token
     const int total = M * nkb;
     const int64_t xrs = p.x_swiglu ? 2 * p.K : p.K;
-    float tmax[QG_MAXM] = {0.f, 0.f, 0.f, 0.f};
-    // 4 blocks per thread per pass, all loads issued before any is used
     for (int base = 0; base < total; base += 4 * QG_THREADS) {
-      uint4 v[4], u[4];
+      uint4 v[4], u[4];  // 4 blocks per thread per pass, all loads issued first
 #pragma unroll
       for (int b = 0; b < 4; b++) {
         const int i = base + b * QG_THREADS + tid;
@@ -304,109 +238,33 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
 #pragma unroll
       for (int b = 0; b < 4; b++) {
         const int i = base + b * QG_THREADS + tid;
-        float sum = 0.f;
-        int t = 0, kb = 0;
-        if (i < total) {
-          t = i / nkb;
-          kb = i - t * nkb;
-          const int64_t k = cg0 * GS + (int64_t)kb * 8;
-          uint4 x8 = v[b];
-          if (p.x_swiglu)
-            x8 = make_uint4(swiglu2(x8.x, u[b].x), swiglu2(x8.y, u[b].y), swiglu2(x8.z, u[b].z),
-                            swiglu2(x8.w, u[b].w));
-          if (p.norm_w) x8 = norm8(x8, xinv[t], p.norm_w + k);
-          const float2 a = __bfloat1622float2(u32_as_bf162(x8.x)), b2 = __bfloat1622float2(u32_as_bf162(x8.y));
-          const float2 c2 = __bfloat1622float2(u32_as_bf162(x8.z)), d2 = __bfloat1622float2(u32_as_bf162(x8.w));
-          sum = ((a.x + a.y) + (b2.x + b2.y)) + ((c2.x + c2.y) + (d2.x + d2.y));
-          const float mx = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b2.x), fabsf(b2.y))),
-                                 fmaxf(fmaxf(fabsf(c2.x), fabsf(c2.y)), fmaxf(fabsf(d2.x), fabsf(d2.y))));
-#pragma unroll
-          for (int q = 0; q < QG_MAXM; q++)
-            if (q == t) tmax[q] = fmaxf(tmax[q], mx);
+        const bool in = i < total;
+        const int t = in ? i / nkb : 0, kb = in ? i - t * nkb : 0;
+        uint4 x8 = v[b];
+        if (in && p.x_swiglu)
+          x8 = make_uint4(swiglu2(x8.x, u[b].x), swiglu2(x8.y, u[b].y), swiglu2(x8.z, u[b].z), swiglu2(x8.w, u[b].w));
+        if (in && p.norm_w) x8 = norm8(x8, xinv[t], p.norm_w + cg0 * GS + (int64_t)kb * 8);
+        const float2 v0 = __bfloat1622float2(u32_as_bf162(x8.x)), v1 = __bfloat1622float2(u32_as_bf162(x8.y));
+        const float2 v2 = __bfloat1622float2(u32_as_bf162(x8.z)), v3 = __bfloat1622float2(u32_as_bf162(x8.w));
+        float sum = ((v0.x + v0.y) + (v1.x + v1.y)) + ((v2.x + v2.y) + (v3.x + v3.y));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // 4 blocks = one 32-value chunk
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (in) {
           *reinterpret_cast<uint4*>(xs + (size_t)t * g.xstr + (size_t)kb * 16) = x8;
+          if ((kb & 3) == 0) xsum[(kb >> 2) * QG_TOKP + t] = sum;
         }
-#pragma unroll
-        for (int o = 1; o < BPG; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (i < total && (kb % BPG) == 0) xsumb[(kb / BPG) * QG_TOKP + t] = sum;
       }
-    }
-#pragma unroll
-    for (int q = 0; q < QG_MAXM; q++) {
-      float m = tmax[q];
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0 && q < M && m > 0.f) atomicMax(&smax[q], __float_as_uint(m));
-    }
-    for (int i = tid; i < ncg * (QG_TOKP - M); i += QG_THREADS) {
-      const int gl = i / (QG_TOKP - M), t = M + (i - gl * (QG_TOKP - M));
-      xsumb[gl * QG_TOKP + t] = 0.f;
-      xsumq[gl * QG_TOKP + t] = 0.f;
-    }
-    __syncthreads();
-    for (int base = 0; base < total; base += QG_THREADS) {
-      const int i = base + tid;
-      float sum = 0.f;
-      int t = 0, kb = 0;
-      if (i < total) {
-        t = i / nkb;
-        kb = i - t * nkb;
-        // 2^s with max |x| 2^s < 2^15 (fp16 max 65504)
-        const uint32_t mb = smax[t];
-        const int e = mb ? (int)((mb >> 23) & 0xFF) - 127 : 0;
-        int sh = 14 - e;
-        sh = sh > 100 ? 100 : (sh < -100 ? -100 : sh);
-        const float f0 = ldexpf(1.f, sh), f1 = BITS == 4 ? ldexpf(1.f, sh - 4) : f0;
-        uint4* px = reinterpret_cast<uint4*>(xs + (size_t)t * g.xstr + (size_t)kb * 16);
-        const uint4 x8 = *px;
-        float2 v0 = __bfloat1622float2(u32_as_bf162(x8.x)), v1 = __bfloat1622float2(u32_as_bf162(x8.y));
-        float2 v2 = __bfloat1622float2(u32_as_bf162(x8.z)), v3 = __bfloat1622float2(u32_as_bf162(x8.w));
-        float2 h0, h1, h2, h3;  // fp16 pairs in MMA operand order
-        if constexpr (BITS == 4) {
-          // (x0,x4)*f0, (x1,x5)*f1, (x2,x6)*f0, (x3,x7)*f1
-          h0 = make_float2(v0.x * f0, v2.x * f0);
-          h1 = make_float2(v0.y * f1, v2.y * f1);
-          h2 = make_float2(v1.x * f0, v3.x * f0);
-          h3 = make_float2(v1.y * f1, v3.y * f1);
-        } else {
-          h0 = make_float2(v0.x * f0, v0.y * f0);
-          h1 = make_float2(v1.x * f0, v1.y * f0);
-          h2 = make_float2(v2.x * f0, v2.y * f0);
-          h3 = make_float2(v3.x * f0, v3.y * f0);
-        }
-        const __half2 q0 = __float22half2_rn(h0), q1 = __float22half2_rn(h1);
-        const __half2 q2 = __float22half2_rn(h2), q3 = __float22half2_rn(h3);
-        const float2 r0 = __half22float2(q0), r1 = __half22float2(q1);
-        const float2 r2 = __half22float2(q2), r3 = __half22float2(q3);
-        sum = ((r0.x + r0.y) + (r1.x + r1.y)) + ((r2.x + r2.y) + (r3.x + r3.y));
-        uint4 o;
-        o.x = *reinterpret_cast<const uint32_t*>(&q0);
-        o.y = *reinterpret_cast<const uint32_t*>(&q1);
-        o.z = *reinterpret_cast<const uint32_t*>(&q2);
-        o.w = *reinterpret_cast<const uint32_t*>(&q3);
-        *px = o;
-        if (kb == 0) xscale[t] = ldexpf(1.f, -sh);
-      }
-#pragma unroll
-      for (int o = 1; o < BPG; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (i < total && (kb % BPG) == 0) xsumq[(kb / BPG) * QG_TOKP + t] = 1024.f * sum;
     }
   }
   __syncthreads();
 
-#ifdef QG_X_TRACE
-  if (lane == 0) atomicAdd(&qg_trace[6], globaltimer() - t_start);
-#endif
   // ---- stream the warp's stages, tile after tile ----
-  const bool tv = gq < M;
-  const uint8_t* xlane = xs + (size_t)(tv ? gq : 0) * g.xstr + (size_t)c * (GS / 4) * 2;
-  int off0[GC][NH], off1[GC][NH];  // lane-constant swizzled offsets of rows gq, gq + 8
+  // lane = (rs, kc): 16-byte chunk kc of each 128-byte stage row, rows rs + 4j of the strip
+  const int rs = lane >> 3, kc = lane & 7;
+  int soff[4];
 #pragma unroll
-  for (int gi = 0; gi < GC; gi++)
-#pragma unroll
-    for (int h = 0; h < NH; h++) {
-      off0[gi][h] = swz(gq, gi * GB + c * LB + 16 * h);
-      off1[gi][h] = swz(gq + 8, gi * GB + c * LB + 16 * h);
-    }
-  const float e0 = 2 * c < M ? xscale[2 * c] : 0.f, e1 = 2 * c + 1 < M ? xscale[2 * c + 1] : 0.f;
+  for (int jr = 0; jr < 4; jr++) soff[jr] = swz(rs + 4 * jr, kc * 16);
+  constexpr int CPG = GB / 16;  // 16-byte chunks per group
   bool ok = true;
   int j = 0, st = 0;
   uint32_t phase = 0;
@@ -415,75 +273,18 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
     uint8_t* scb = smem + L.o_sc + (size_t)(ti & 1) * scbuf;
     cp_async_wait1();  // this tile's scales (all but the newest copy group)
     __syncthreads();   // ... visible to every thread; the previous tile's reduction is done
-    const bf16* sc0 = reinterpret_cast<const bf16*>(scb + (size_t)(s * 16 + gq) * g.sbrow);
-    const bf16* sc1 = reinterpret_cast<const bf16*>(scb + (size_t)(s * 16 + gq + 8) * g.sbrow);
-    const bf16* bi0 = reinterpret_cast<const bf16*>(scb + (size_t)(rows + s * 16 + gq) * g.sbrow);
-    const bf16* bi1 = reinterpret_cast<const bf16*>(scb + (size_t)(rows + s * 16 + gq + 8) * g.sbrow);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};   // scale * (sum(x' code) - Q), x' domain
-    float accb[4] = {0.f, 0.f, 0.f, 0.f};  // bias * X
+    float res[4][MT];
+#pragma unroll
+    for (int jr = 0; jr < 4; jr++)
+#pragma unroll
+      for (int t = 0; t < MT; t++) res[jr][t] = 0.f;
     for (int jj = 0; jj < nch; jj++, j++) {  // j: this warp's stage counter
-
-#ifdef QG_X_TRACE
-      const uint64_t t_a = globaltimer();
-#endif
       ok &= mbar_wait(&bars[st], phase);
-#ifdef QG_X_TRACE
-      const uint64_t t_b = globaltimer();
-      if (lane == 0) { atomicAdd(&qg_trace[0], t_b - t_a); atomicAdd(&qg_trace[1], 1ull); }
-#endif
       const uint8_t* stg = ring + st * QG_STAGE_BYTES;
+      uint4 wv[4];
 #pragma unroll
-      for (int gi = 0; gi < GC; gi++) {
-        if (jj * GC + gi < nwg) {
-          const int gl = wg0 + jj * GC + gi;
-          uint32_t w0[WL], w1[WL];
-#pragma unroll
-          for (int h = 0; h < NH; h++) {
-            lds_lane<LBH>(stg + off0[gi][h], *reinterpret_cast<uint32_t(*)[LBH / 4]>(w0 + h * 4));
-            lds_lane<LBH>(stg + off1[gi][h], *reinterpret_cast<uint32_t(*)[LBH / 4]>(w1 + h * 4));
-          }
-          float ag[4] = {0.f, 0.f, 0.f, 0.f};
-          const uint8_t* xp = xlane + (size_t)gl * GS * 2;
-          if constexpr (BITS == 4) {
-#pragma unroll
-            for (int wi = 0; wi < WL; wi++) {
-              uint32_t pa[4], pb[4];
-              unpack4h(w0[wi], pa);
-              unpack4h(w1[wi], pb);
-              uint4 xv = make_uint4(0, 0, 0, 0);
-              if (tv) xv = *reinterpret_cast<const uint4*>(xp + wi * 16);
-              const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]};
-              const uint32_t a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-              mma_f16_16816(ag, a0, xv.x, xv.y);
-              mma_f16_16816(ag, a1, xv.z, xv.w);
-            }
-          } else {
-#pragma unroll
-            for (int wi = 0; wi < WL; wi++) {
-              uint32_t pa[2], pb[2];
-              unpack8h(w0[wi], pa);
-              unpack8h(w1[wi], pb);
-              uint2 xv = make_uint2(0, 0);
-              if (tv) xv = *reinterpret_cast<const uint2*>(xp + wi * 8);
-              const uint32_t a[4] = {pa[0], pb[0], pa[1], pb[1]};
-              mma_f16_16816(ag, a, xv.x, xv.y);
-            }
-          }
-          const float s0 = __bfloat162float(sc0[gl]), s1 = __bfloat162float(sc1[gl]);
-          const float b0 = __bfloat162float(bi0[gl]), b1 = __bfloat162float(bi1[gl]);
-          const float2 xq = *reinterpret_cast<const float2*>(xsumq + gl * QG_TOKP + 2 * c);
-          const float2 xb = *reinterpret_cast<const float2*>(xsumb + gl * QG_TOKP + 2 * c);
-          acc[0] = fmaf(s0, ag[0] - xq.x, acc[0]);
-          acc[1] = fmaf(s0, ag[1] - xq.y, acc[1]);
-          acc[2] = fmaf(s1, ag[2] - xq.x, acc[2]);
-          acc[3] = fmaf(s1, ag[3] - xq.y, acc[3]);
-          accb[0] = fmaf(b0, xb.x, accb[0]);
-          accb[1] = fmaf(b0, xb.y, accb[1]);
-          accb[2] = fmaf(b1, xb.x, accb[2]);
-          accb[3] = fmaf(b1, xb.y, accb[3]);
-        }
-      }
-      // refill this stage once every lane has read it (generic reads before the async write)
+      for (int jr = 0; jr < 4; jr++) wv[jr] = *reinterpret_cast<const uint4*>(stg + soff[jr]);
+      // refill this stage now that every lane has read it (generic reads before the async write)
       __syncwarp();
       if (lane == 0 && j + QG_STAGES < total_st) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -493,17 +294,85 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
         st = 0;
         phase ^= 1u;
       }
+      const int cw = jj * GC * CPG + kc;  // chunk index inside the warp's range
+      if (cw < nwg * CPG) {
+        const int chl = wg0 * CPG + cw;  // chunk index inside the CTA's range
+        const int gl = chl / CPG;
+        // x of the chunk for every token as bf16 pairs (x[2i], x[2i+1])
+        uint32_t xw[MT][16];
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+          const uint4* xp = reinterpret_cast<const uint4*>(xs + (size_t)t * g.xstr + (size_t)chl * 64);
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const uint4 xv = xp[q];
+            xw[t][4 * q] = xv.x; xw[t][4 * q + 1] = xv.y; xw[t][4 * q + 2] = xv.z; xw[t][4 * q + 3] = xv.w;
+          }
+        }
+        unsigned long long sacc[4][MT];
+#pragma unroll
+        for (int jr = 0; jr < 4; jr++)
+#pragma unroll
+          for (int t = 0; t < MT; t++) sacc[jr][t] = 0ull;
+#pragma unroll
+        for (int wi = 0; wi < 4; wi++) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            // x pair (x[8wi+2i], x[8wi+2i+1]) for each token
+            unsigned long long xp2[MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+              const uint32_t w2 = xw[t][wi * 4 + i];
+              xp2[t] = pack_u2(w2 << 16, w2 & 0xFFFF0000u);
+            }
+#pragma unroll
+            for (int jr = 0; jr < 4; jr++) {
+              const uint32_t w = wi == 0 ? wv[jr].x : wi == 1 ? wv[jr].y : wi == 2 ? wv[jr].z : wv[jr].w;
+              const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+              // (128 + q) as exact fp32 for nibbles 2i, 2i+1: bytes [0, 0, q, 0x43]
+              const uint32_t fl = prmt(lo, 0x43000000u, 0x7044u | (i << 8));
+              const uint32_t fh = prmt(hi, 0x43000000u, 0x7044u | (i << 8));
+              const unsigned long long wp = pack_u2(fl, fh);
+#pragma unroll
+              for (int t = 0; t < MT; t++) ffma2(sacc[jr][t], wp, xp2[t]);
+            }
+          }
+        }
+        // fold the chunk: scale * sum(x (128 + q)) + (bias - 128 scale) * sum(x)
+#pragma unroll
+        for (int jr = 0; jr < 4; jr++) {
+          const int r = s * 16 + rs + 4 * jr;
+          const float sv = __bfloat162float(*reinterpret_cast<const bf16*>(scb + (size_t)r * g.sbrow + gl * 2));
+          const float bv = fmaf(-128.f, sv,
+                                __bfloat162float(*reinterpret_cast<const bf16*>(scb + (size_t)(rows + r) * g.sbrow + gl * 2)));
+#pragma unroll
+          for (int t = 0; t < MT; t++) {
+            const float2 sp = unpack_f2(sacc[jr][t]);
+            res[jr][t] = fmaf(sv, sp.x + sp.y, fmaf(bv, xsum[chl * QG_TOKP + t], res[jr][t]));
+          }
+        }
+      }
+    }
+    // the 8 chunk lanes of each row, then res -> red[warp][row][token]
+#pragma unroll
+    for (int jr = 0; jr < 4; jr++)
+#pragma unroll
+      for (int t = 0; t < MT; t++) {
+        float v = res[jr][t];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        res[jr][t] = v;
+      }
+    if (kc == 0) {
+      float* rw = red + (size_t)warp * 16 * QG_TOKP;
+#pragma unroll
+      for (int jr = 0; jr < 4; jr++)
+#pragma unroll
+        for (int t = 0; t < MT; t++) rw[(rs + 4 * jr) * QG_TOKP + t] = res[jr][t];
     }
 
     // ---- fixed-order reduction: warps of the CTA, then the CTAs of the cluster ----
-    // back from the x' domain (y = 2^-s acc + accb): (row gq / gq+8, tokens 2c, 2c+1)
-    {
-      float* rw = red + (size_t)warp * 16 * QG_TOKP;
-      *reinterpret_cast<float2*>(rw + gq * QG_TOKP + 2 * c) =
-          make_float2(fmaf(acc[0], e0, accb[0]), fmaf(acc[1], e1, accb[1]));
-      *reinterpret_cast<float2*>(rw + (gq + 8) * QG_TOKP + 2 * c) =
-          make_float2(fmaf(acc[2], e0, accb[2]), fmaf(acc[3], e1, accb[3]));
-    }
     __syncthreads();
     // the buffer of this tile's scales is free: start copying the scales two tiles ahead
     qg_load_scales(p, g, scb, (cluster_id + (ti + 2) * nclusters) * rows, KG, cg0, ncg, ti + 2 < ntl, tid);
@@ -553,24 +422,28 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-#ifdef QG_X_TRACE
-  if (lane == 0) { atomicAdd(&qg_trace[2], globaltimer() - t_start); atomicAdd(&qg_trace[3], 1ull); }
-  if (tid == 0) atomicMax(&qg_trace[4], globaltimer());
-  if (tid == 0) atomicMin(&qg_trace[5], t_start);
-#endif
   if (!ok && p.status) atomicExch(p.status, VMLX_E_STATE);
 }
 
 // ---- host side -------------------------------------------------------------
 
+// Tuning overrides read once per process: VMLX_QG (force this kernel on / off),
+// VMLX_QG_S / VMLX_QG_C (force the strips per tile / the cluster size).
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return v && *v ? atoi(v) : dflt;
 }
+static int env_cached(int which) {
+  static const int vals[3] = {env_int("VMLX_QG", -1), env_int("VMLX_QG_S", 0), env_int("VMLX_QG_C", 0)};
+  return vals[which];
+}
 
-static int qg_per_sm(const QgSmem& L) {
+// Resident CTAs per SM: shared memory, and registers (up to 128 per thread: 2 CTAs of 256).
+static int qg_per_sm(const QgSmem& L, int m = QG_MAXM) {
   int per = (int)((228 * 1024) / (L.total + 1024));
-  return per > 3 ? 3 : per;  // 80 registers x 256 threads: 3 CTAs per SM
+  const int reg_cap = 2;
+  (void)m;
+  return per > reg_cap ? reg_cap : per;
 }
 
 static void qg_fill(QgGeom& gm, int64_t N, int64_t K, int gs, int S, int C) {
@@ -582,6 +455,7 @@ static void qg_fill(QgGeom& gm, int64_t N, int64_t K, int gs, int S, int C) {
   gm.KGC = KGC;
   gm.xstr = KGC * gs * 2 + 16;
   gm.sbrow = KGC * 2 + 16;
+  gm.cpg = gs / 32;
   gm.ntiles = (int)((N + 16 * S - 1) / (16 * S));
 }
 
@@ -593,7 +467,7 @@ static bool qg_choose(int64_t N, int64_t K, int bits, int gs, QgGeom& best) {
   const int64_t KG = K / gs;
   const int GC = 128 / (gs * bits / 8);
   const int sms = sm_count();
-  const int forceS = env_int("VMLX_QG_S", 0), forceC = env_int("VMLX_QG_C", 0);
+  const int forceS = env_cached(1), forceC = env_cached(2);
   double best_cost = 1e30;
   bool found = false;
   for (int C = 1; C <= QG_MAX_CLUSTER; C++) {
@@ -627,8 +501,9 @@ static bool qg_choose(int64_t N, int64_t K, int bits, int gs, QgGeom& best) {
   return found;
 }
 
-template <int BITS, int GS>
+template <int GS, int MT>
 static int launch_qg(const QmvArgs& a, cudaStream_t st) {
+  constexpr int BITS = 4;
   QgGeom g;
   if (!qg_choose(a.N, a.K, BITS, GS, g))
     return set_error(VMLX_E_UNSUPPORTED, "qgemv: no launch geometry for N=%lld K=%lld", (long long)a.N,
@@ -636,14 +511,12 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
   g.sc_async = (a.K / GS) % 8 == 0 && aligned(a.scales, 16) && aligned(a.biases, 16);
   QgSmem L;
   L.init(g, (int)a.M);
-  auto kern = qgemv_kernel<BITS, GS>;
+  auto kern = qgemv_kernel<GS, MT>;
   {
     const int rc = ensure_max_dynamic_smem((const void*)kern, 220 * 1024);
     if (rc) return rc;
   }
-  QgSmem Lmax;
-  Lmax.init(g, QG_MAXM);
-  const int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(Lmax) / g.C);
+  const int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(L, MT) / g.C);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(nclu * g.C), 1, 1);
   cfg.blockDim = dim3(QG_THREADS);
@@ -676,20 +549,32 @@ bool qgemv_covers(const QmvArgs& a, int mode, int bits, int gs) {
   if (a.M < 1 || a.M > QG_MAXM) return false;
   if (a.K % 8 || a.N >= (1LL << 31)) return false;
   if (!aligned(a.x, 16) || (a.norm_w && !aligned(a.norm_w, 16))) return false;
-  if (!env_int("VMLX_QG", 0) || env_int("VMLX_QG_DISABLE", 0)) return false;
-  (void)bits;
+  if (bits != 4) return false;
+  // By shape, never by M (one kernel per (N, K) keeps rows batch-invariant across M = 1..4):
+  // measured on B200 (CUDA graph, rotated weights > L2), this kernel wins on matrices up to
+  // ~8K x 8K; the ring-and-cluster kernel of qmv.cu keeps the larger ones, where its deeper
+  // K split hides more latency.  VMLX_QG=1 / 0 forces the choice.
   (void)gs;
-  return true;
+  const int force = env_cached(0);
+  if (force >= 0) return force != 0;
+  return a.N >= 1024 && a.N <= 8192 && a.K <= 8192;
+}
+
+template <int GS>
+static int launch_qg_m(const QmvArgs& a, cudaStream_t st) {
+  switch (a.M) {
+    case 1: return launch_qg<GS, 1>(a, st);
+    case 2: return launch_qg<GS, 2>(a, st);
+    case 3: return launch_qg<GS, 3>(a, st);
+    default: return launch_qg<GS, 4>(a, st);
+  }
 }
 
 int launch_qgemv(const QmvArgs& a, int bits, int gs, cudaStream_t st) {
-  if (bits == 4 && gs == 32) return launch_qg<4, 32>(a, st);
-  if (bits == 4 && gs == 64) return launch_qg<4, 64>(a, st);
-  if (bits == 4 && gs == 128) return launch_qg<4, 128>(a, st);
-  if (bits == 8 && gs == 32) return launch_qg<8, 32>(a, st);
-  if (bits == 8 && gs == 64) return launch_qg<8, 64>(a, st);
-  if (bits == 8 && gs == 128) return launch_qg<8, 128>(a, st);
-  return set_error(VMLX_E_UNSUPPORTED, "matmul: bits=%d group_size=%d not supported", bits, gs);
+  if (bits == 4 && gs == 32) return launch_qg_m<32>(a, st);
+  if (bits == 4 && gs == 64) return launch_qg_m<64>(a, st);
+  if (bits == 4 && gs == 128) return launch_qg_m<128>(a, st);
+  return set_error(VMLX_E_UNSUPPORTED, "qgemv: bits=%d group_size=%d not supported", bits, gs);
 }
 
 }  // namespace vmlx
