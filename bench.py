@@ -477,6 +477,8 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
     xh = x0.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
     n_e2e = max(8, args.steps // 2)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(n_e2e):

@@ -100,8 +100,9 @@ VMLX_API int vmlx_cuda_dequantize(void* out, int out_dtype, const uint32_t* wq, 
  * y [M, N] = x [M, K] @ dequantize(w [N, K])^T, bf16 in/out, fp32 accumulation.
  * Replaces mlx_quantized_matmul (Source/Cmlx/include/mlx/c/ops.h:809-819), the
  * op behind QuantizedLinear.callAsFunction (Source/MLXNN/Quantized.swift:361-376).
- * biases may not be NULL for mode "affine".  M <= 32 runs the decode GEMV
- * kernel; larger M runs the tensor-core (tcgen05) GEMM.
+ * biases may not be NULL for mode "affine".  M <= 4 runs a decode GEMV kernel
+ * (fp32 accumulation over exact codes); M >= 5 runs the tensor-core (tcgen05) GEMM,
+ * which, like the reference's affine_qmm_t, multiplies bf16-dequantized weights.
  */
 VMLX_API int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t* w, const void* scales,
                                const void* biases, bool transpose, int group_size, int bits,

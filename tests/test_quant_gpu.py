@@ -166,7 +166,9 @@ def test_quantized_mm_gemv(vm, orc, cuda, bits, gs, M):
     rng = np.random.default_rng(5 + M)
     xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
     y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=gs, bits=bits)
-    ref = orc.qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), gs, bits)
+    # M <= 4: GEMV over exact codes; M >= 5: tcgen05 GEMM over bf16-dequantized tiles (affine_qmm_t)
+    qmm = orc.qmm_f64 if M <= 4 else orc.qmm_bf16w_f64
+    ref = qmm(xb, u32(wq), bits_of(s), bits_of(b), gs, bits)
     check_close(y.float().cpu().numpy(), ref)
 
 
@@ -179,7 +181,7 @@ def test_quantized_mm_llama_ffn_shapes(vm, orc, cuda, M):
         xb = orc.f32_to_bf16(rng.normal(0, 1, (M, K)).astype(np.float32))
         y = vm.quantized_mm(to_dev_bf16(orc, xb, cuda), wq, s, b, group_size=64, bits=4)
         rows = np.arange(0, N, 37)  # the fp64 oracle on a sample of output columns
-        qmm = orc.qmm_f64 if M <= 32 else orc.qmm_bf16w_f64  # GEMV vs tiled-GEMM semantics
+        qmm = orc.qmm_f64 if M <= 4 else orc.qmm_bf16w_f64  # GEMV vs tiled-GEMM semantics
         ref = qmm(xb, u32(wq)[rows], bits_of(s)[rows], bits_of(b)[rows], 64, 4)
         check_close(y.float().cpu().numpy()[:, rows], ref)
 
@@ -228,8 +230,8 @@ def test_tensor_core_fallback_shape(vm, orc, cuda):
 def test_batch_invariance(vm, orc, cuda):
     """QuantizedSmallMScalingBenchTests.swift:110-127: M rows at once must equal
     M single-row calls exactly (maxDiff == 0), 4-bit g64 bf16, M=4.  The
-    kernel has two regimes (CUDA-core for M <= 4, tensor-core MMA for 5..32);
-    inside each, a row's result does not depend on the other rows."""
+    op has two regimes below 65 rows (the GEMV for M <= 4, the tcgen05 GEMM
+    for 5..64); inside each, a row's result does not depend on the other rows."""
     K, N = 5120, 1024
     wb, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 41)
     x = torch.randn(32, K, device=cuda, generator=torch.Generator(cuda).manual_seed(0)).bfloat16()

@@ -20,6 +20,18 @@ static int check_mm_args(const void* y, const void* x, const void* w, const void
   return VMLX_OK;
 }
 
+// Smallest M that runs on the tensor-core GEMM (VMLX_TC_MIN_M overrides; read once).
+// From 5 rows up the tcgen05 GEMM is the faster kernel on every Llama-shaped matrix but
+// the small ones at 8 rows (the warp-level mma.sync of the GEMV kernel runs far below
+// HBM speed at 16-32 rows on B200); one kernel for 5..32 rows keeps them batch-invariant.
+static int64_t tc_min_m() {
+  static const int64_t v = [] {
+    const char* e = getenv("VMLX_TC_MIN_M");
+    return (int64_t)(e && *e ? atoll(e) : 5);
+  }();
+  return v;
+}
+
 static int toka_for(int64_t m) { return (int)(m < 1 ? 1 : (m > 32 ? 32 : m)); }
 
 }  // namespace vmlx
@@ -34,7 +46,7 @@ extern "C" int vmlx_cuda_quantized_matmul(void* y, const void* x, const uint32_t
   int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
   if (rc) return rc;
   cudaStream_t st = as_stream(stream);
-  if (M > 32) {
+  if (M >= tc_min_m()) {
     bool handled = false;
     rc = launch_qmm_tc((const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, M, N, K,
                        bits, group_size, st, &handled);

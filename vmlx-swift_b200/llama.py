@@ -136,7 +136,9 @@ class LlamaDecoder:
             self.all_sum = group.all_sum
         # fused: RMSNorm folded into the q/k/v and gate/up GEMVs (x staged normalised), and at TP=1
         # the residual adds folded into the o_proj / down_proj GEMVs (in place on x)
-        self.fused = fused and batch <= 32
+        # (decode rows 1-4 run the GEMV kernels that carry the fusions; from 5 rows the linears
+        # run on the tensor-core GEMM and the norms / adds as their own kernels)
+        self.fused = fused and batch <= 4
         self.hq, self.hkv, self.ffn = cfg.n_heads // world, cfg.n_kv_heads // world, cfg.ffn // world
         gen = torch.Generator(device=dev).manual_seed(seed)
         self.layers = [LlamaLayerWeights(cfg, dev, gen, rank, world) for _ in range(cfg.n_layers)]
