@@ -162,6 +162,24 @@ VMLX_API int vmlx_cuda_gather_qmm(void* y, const void* x, const uint32_t* w, con
                          int64_t M, int64_t N, int64_t K, int64_t n_experts, void* stream);
 
 
+/*
+ * vmlx_cuda_gather_qmm with a caller-owned device workspace (256-byte aligned, at least
+ * vmlx_cuda_gather_qmm_workspace_size(batch, M, K, n_experts) bytes).  A sorted gather
+ * (sorted_indices, rhs_indices given, n_experts <= 1024, K a multiple of 64) with on
+ * average >= 8 rows per expert runs as an expert-segmented tcgen05 GEMM: one 64-row tile per
+ * run of equal experts, bf16-dequantized weights, as affine_gather_qmm_rhs
+ * (quantized.h:2197-2391).  Anything else, or a too-small workspace, runs
+ * vmlx_cuda_gather_qmm unchanged.  Same argument order as mlx_gather_qmm (ops.h:475-488)
+ * plus the workspace.
+ */
+VMLX_API size_t vmlx_cuda_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t n_experts);
+VMLX_API int vmlx_cuda_gather_qmm_ws(void* y, const void* x, const uint32_t* w, const void* scales,
+                                     const void* biases, const uint32_t* lhs_indices,
+                                     const uint32_t* rhs_indices, bool transpose, int group_size, int bits,
+                                     const char* mode, bool sorted_indices, int64_t batch, int64_t x_batches,
+                                     int64_t M, int64_t N, int64_t K, int64_t n_experts, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* ---- MoE routing around SwitchGLU ---- */
 
 /*

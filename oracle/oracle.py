@@ -171,12 +171,14 @@ def qmm_fp32_bf16(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarr
     return y
 
 
-def gather_qmm_f64(x_bf16, wq, scales, biases, lhs, rhs, group_size=64, bits=4) -> np.ndarray:
+def gather_qmm_f64(x_bf16, wq, scales, biases, lhs, rhs, group_size=64, bits=4, bf16w=False) -> np.ndarray:
     """y[b] = x[lhs[b]] @ deq(W[rhs[b]])^T in fp64 (quantized.h:1438-1491 semantics).
 
     x [xb, M, K] bf16 bits; W [E, N, K/pf].  lhs None: batch b reads x batch
     b*xb/nb.  Each routed expert is dequantized once (C oracle, exact fp32) and
-    all batch elements routed to it are multiplied in one fp64 matmul."""
+    all batch elements routed to it are multiplied in one fp64 matmul.  bf16w: the
+    tiled kernels' semantics (affine_gather_qmm_rhs, quantized.h:2197-2391, like
+    qmm_bf16w_f64): each weight rounded once to bf16 first."""
     x = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16)).astype(np.float64)
     xb, M, K = x.shape
     E, N = wq.shape[0], wq.shape[1]
@@ -188,7 +190,8 @@ def gather_qmm_f64(x_bf16, wq, scales, biases, lhs, rhs, group_size=64, bits=4) 
         if e < 0 or e >= E:
             continue
         sel = np.nonzero(rhs == e)[0]
-        w = dequantize(wq[e], scales[e], biases[e], group_size, bits).astype(np.float64)
+        w = dequantize(wq[e], scales[e], biases[e], group_size, bits)
+        w = (round_bf16(w) if bf16w else w).astype(np.float64)
         y[sel] = np.einsum("bmk,nk->bmn", x[lhs_a[sel]], w)
     return y
 
@@ -211,20 +214,23 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
-def switch_glu(x_bf16, gate, up, down, indices, group_size=64, bits=4) -> np.ndarray:
+def switch_glu(x_bf16, gate, up, down, indices, group_size=64, bits=4, bf16w=None) -> np.ndarray:
     """Reference SwitchGLU forward: x [T, D] bf16 bits, indices [T, k];
     gate/up/down = (wq, scales, biases) stacks.  Returns float64 [T, k, D].
     Intermediate activations are rounded to bf16 where the reference holds
-    bf16 arrays (gate/up outputs, silu(g)*u)."""
+    bf16 arrays (gate/up outputs, silu(g)*u).  bf16w (default: T*k >= 64, the
+    sorted path, and >= 8 rows per expert) selects the tiled kernels' bf16 weights."""
     T, D = x_bf16.shape
     k = indices.shape[1]
     rhs = indices.reshape(-1).astype(np.uint32)
     xb = x_bf16.reshape(T, 1, D)
     lhs = np.repeat(np.arange(T), k).astype(np.uint32)
-    g = round_bf16(gather_qmm_f64(xb, *gate, lhs, rhs, group_size, bits).astype(np.float32))
-    u = round_bf16(gather_qmm_f64(xb, *up, lhs, rhs, group_size, bits).astype(np.float32))
+    if bf16w is None:
+        bf16w = T * k >= 64 and T * k >= 8 * gate[0].shape[0]
+    g = round_bf16(gather_qmm_f64(xb, *gate, lhs, rhs, group_size, bits, bf16w).astype(np.float32))
+    u = round_bf16(gather_qmm_f64(xb, *up, lhs, rhs, group_size, bits, bf16w).astype(np.float32))
     act = f32_to_bf16(round_bf16(silu(g.astype(np.float64)).astype(np.float32)) * u)
-    y = gather_qmm_f64(act.reshape(T * k, 1, -1), *down, None, rhs, group_size, bits)
+    y = gather_qmm_f64(act.reshape(T * k, 1, -1), *down, None, rhs, group_size, bits, bf16w)
     return y.reshape(T, k, -1)
 
 

@@ -112,3 +112,30 @@ def test_moe_block_config4_128_experts(vm, orc, cuda, T):
            scores.cpu().numpy().astype(np.float64)[:, :, None]).sum(1)
     assert out.shape == (T, D)
     check_close(out.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("case", ["sorted_lhs", "many_rows", "out_of_range"])
+def test_sorted_gather_tensor_core(vm, orc, cuda, case):
+    """Sorted gather_qmm with a workspace runs the expert-segmented tcgen05 GEMM
+    (affine_gather_qmm_rhs semantics: bf16 weights): experts with > 64 rows (several
+    tiles), x rows through lhs_indices, and ids >= n_experts (rows left zero)."""
+    E, N, K = 16, 320, 512
+    _, (wq, s, b) = make_weights(orc, vm, cuda, N, K, 64, 4, 91, lead=(E,))
+    rng = np.random.default_rng(92)
+    P = 400
+    rhs = np.sort(rng.integers(0, E, P)).astype(np.int64)
+    if case == "many_rows":
+        rhs = np.sort(np.concatenate([np.full(150, 3), rng.integers(0, E, P - 150)])).astype(np.int64)
+    if case == "out_of_range":
+        rhs[-5:] = E + 2
+    xb = orc.f32_to_bf16(rng.normal(0, 1, (P, 1, K)).astype(np.float32))
+    lhs = rng.permutation(P).astype(np.int64) if case == "sorted_lhs" else None
+    ws = torch.empty(vm.ops.gather_qmm_workspace_size(P, 1, K, E), dtype=torch.uint8, device=cuda)
+    x = to_dev_bf16(orc, xb, cuda)
+    li = torch.from_numpy(lhs).to(cuda) if lhs is not None else None
+    ri = torch.from_numpy(rhs).to(cuda)
+    y = vm.gather_quantized_mm(x, wq, s, b, lhs_indices=li, rhs_indices=ri, sorted_indices=True, workspace=ws)
+    ref = orc.gather_qmm_f64(xb, u32(wq), bits_of(s), bits_of(b), lhs, rhs, 64, 4, bf16w=True)
+    check_close(y.float().cpu().numpy(), ref)
+    if case == "out_of_range":
+        assert torch.count_nonzero(y[-5:]) == 0

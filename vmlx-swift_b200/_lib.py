@@ -47,6 +47,10 @@ SIGNATURES = {
     "vmlx_cuda_gather_qmm": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _bool, _int, _int, _str, _bool, _i64, _i64,
                _i64, _i64, _i64, _i64, _vp]),
+    "vmlx_cuda_gather_qmm_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "vmlx_cuda_gather_qmm_ws": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _bool, _int, _int, _str, _bool, _i64, _i64,
+               _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "vmlx_cuda_moe_route": (_int, [_vp, _int, _i64, _int, _int, _bool, _vp, _vp, _vp]),
     "vmlx_cuda_moe_sort": (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     "vmlx_cuda_moe_combine": (_int, [_vp, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp]),

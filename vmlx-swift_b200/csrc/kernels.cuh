@@ -59,4 +59,16 @@ int launch_qmv(const QmvArgs& a, int mode, int bits, int gs, int64_t zcount, int
 int launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y,
                   int64_t M, int64_t N, int64_t K, int bits, int gs, cudaStream_t st, bool* handled);
 
+// Expert-segmented tcgen05 GEMM (sorted gather_qmm): slots {expert, first row, rows}.
+int launch_qmm_tc_grouped(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y,
+                          int64_t M, int64_t N, int64_t K, int64_t n_experts, const int4* slots, int64_t n_slots,
+                          int bits, int gs, cudaStream_t st);
+// Sorted gather_qmm on the tensor cores: row gather + slots + grouped GEMM, in `ws`
+// (gather_tc_workspace bytes).
+size_t gather_tc_workspace(int64_t batch, int64_t M, int64_t K, int64_t n_experts);
+int launch_gather_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases,
+                     const uint32_t* lhs, const uint32_t* rhs, bf16* y, int64_t batch, int64_t x_batches,
+                     int64_t M, int64_t N, int64_t K, int64_t n_experts, int bits, int gs, void* ws,
+                     cudaStream_t st);
+
 }  // namespace vmlx

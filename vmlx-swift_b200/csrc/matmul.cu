@@ -120,3 +120,34 @@ extern "C" int vmlx_cuda_quantized_matmul_swiglu(void* y, const void* gate_up, c
   return launch_qmv(a, QMV_DENSE, bits, group_size, 1, toka_for(M), as_stream(stream));
 }
 
+
+extern "C" size_t vmlx_cuda_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t n_experts) {
+  if (batch <= 0 || M <= 0 || K <= 0 || n_experts <= 0) return 0;
+  return gather_tc_workspace(batch, M, K, n_experts);
+}
+
+// vmlx_cuda_gather_qmm with a caller-owned workspace: sorted gathers with enough rows per
+// expert (on average >= 8) run as an expert-segmented tcgen05 GEMM -- one 64-row tile per
+// run of equal experts, each expert's weights dequantized once per tile, the reference's
+// affine_gather_qmm_rhs (quantized.h:2197-2391) -- instead of the GEMV kernel.
+extern "C" int vmlx_cuda_gather_qmm_ws(void* y, const void* x, const uint32_t* w, const void* scales,
+                                       const void* biases, const uint32_t* lhs_indices,
+                                       const uint32_t* rhs_indices, bool transpose, int group_size, int bits,
+                                       const char* mode, bool sorted_indices, int64_t batch, int64_t x_batches,
+                                       int64_t M, int64_t N, int64_t K, int64_t n_experts, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  const bool tc = sorted_indices && rhs_indices && workspace && batch > 0 && M > 0 && n_experts <= 1024 &&
+                  workspace_bytes >= gather_tc_workspace(batch, M, K, n_experts) && batch * M >= 8 * n_experts &&
+                  K % 64 == 0 && batch * M < (1LL << 30) && aligned(workspace, 256);
+  if (!tc)
+    return vmlx_cuda_gather_qmm(y, x, w, scales, biases, lhs_indices, rhs_indices, transpose, group_size, bits, mode,
+                                sorted_indices, batch, x_batches, M, N, K, n_experts, stream);
+  int rc = check_mm_args(y, x, w, scales, biases, transpose, group_size, bits, mode, M, N, K);
+  if (rc) return rc;
+  if (batch % x_batches && !lhs_indices)
+    return set_error(VMLX_E_INVALID, "without lhs_indices, batch=%lld must be a multiple of x_batches=%lld",
+                     (long long)batch, (long long)x_batches);
+  return launch_gather_tc((const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, lhs_indices, rhs_indices,
+                          (bf16*)y, batch, x_batches, M, N, K, n_experts, bits, group_size, workspace,
+                          as_stream(stream));
+}

@@ -197,6 +197,89 @@ __global__ void moe_combine_kernel(const bf16* __restrict__ y, const uint32_t* _
   for (int q = 0; q < 8 && d0 + q < D; q++) out[t * D + d0 + q] = __float2bfloat16_rn(acc[q]);
 }
 
+
+// ---- sorted gather_qmm on the tensor cores: slots and row gather ----------------------
+
+// Slots of the expert-segmented GEMM: rows (b, m) of a sorted gather (rhs non-decreasing,
+// M rows per batch element) are grouped by expert into tiles of <= QMM_SLOT_ROWS rows:
+// slot = {expert, first row, rows}; the first `cap` entries are written, unused ones
+// with rows = 0.  One CTA; a thread per expert (binary search of its run in rhs) and a
+// shared-memory scan of the per-expert slot counts.
+constexpr int QMM_SLOT_ROWS = 64;
+__global__ void __launch_bounds__(1024) qmm_slots_kernel(const uint32_t* __restrict__ rhs, int64_t batch, int64_t M,
+                                                         int E, int4* __restrict__ slots, int64_t cap) {
+  __shared__ int scan[1024];
+  const int tid = threadIdx.x;
+  int64_t lo = 0, hi = 0;
+  int ns = 0;
+  if (tid < E) {
+    int64_t a = 0, b = batch;
+    while (a < b) { const int64_t mid = (a + b) >> 1; if (rhs[mid] < (uint32_t)tid) a = mid + 1; else b = mid; }
+    lo = a;
+    b = batch;
+    while (a < b) { const int64_t mid = (a + b) >> 1; if (rhs[mid] < (uint32_t)tid + 1) a = mid + 1; else b = mid; }
+    hi = a;
+    ns = (int)(((hi - lo) * M + QMM_SLOT_ROWS - 1) / QMM_SLOT_ROWS);
+  }
+  scan[tid] = ns;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
+    const int v = tid >= o ? scan[tid - o] : 0;
+    __syncthreads();
+    scan[tid] += v;
+    __syncthreads();
+  }
+  const int total = scan[1023];
+  const int first = scan[tid] - ns;
+  for (int j = 0; j < ns; j++) {
+    const int64_t r0 = lo * M + (int64_t)j * QMM_SLOT_ROWS, r1 = hi * M;
+    if (first + j < cap)
+      slots[first + j] = make_int4(tid, (int)r0, (int)(r1 - r0 < QMM_SLOT_ROWS ? r1 - r0 : QMM_SLOT_ROWS), 0);
+  }
+  for (int64_t i = total + tid; i < cap; i += 1024) slots[i] = make_int4(0, 0, 0, 0);
+}
+
+// xs[b*M + m] = x[(lhs ? lhs[b] : b*x_batches/batch)*M + m] (bf16 rows of K), and y rows of
+// batch elements whose expert id is out of range set to zero (no slot covers them).
+__global__ void gather_rows_kernel(const bf16* __restrict__ x, const uint32_t* __restrict__ lhs, int64_t x_batches,
+                                   int64_t batch, int64_t M, int64_t K, const uint32_t* __restrict__ rhs, int E,
+                                   bf16* __restrict__ xs, bf16* __restrict__ y, int64_t N) {
+  const int64_t r = blockIdx.x, b = r / M, m = r - b * M;
+  if (xs) {
+    const int64_t xi = lhs ? (int64_t)lhs[b] : b * x_batches / batch;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (xi * M + m) * K);
+    uint4* dst = reinterpret_cast<uint4*>(xs + r * K);
+    for (int64_t i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
+  }
+  if (rhs[b] >= (uint32_t)E)
+    for (int64_t i = threadIdx.x; i < N; i += blockDim.x) y[r * N + i] = __float2bfloat16_rn(0.f);
+}
+
+size_t gather_tc_workspace(int64_t batch, int64_t M, int64_t K, int64_t n_experts) {
+  const int64_t cap = n_experts + (batch * M + QMM_SLOT_ROWS - 1) / QMM_SLOT_ROWS;
+  return (size_t)((cap * 16 + 255) / 256 * 256) + (size_t)batch * M * K * 2;
+}
+
+int launch_gather_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases,
+                     const uint32_t* lhs, const uint32_t* rhs, bf16* y, int64_t batch, int64_t x_batches,
+                     int64_t M, int64_t N, int64_t K, int64_t n_experts, int bits, int gs, void* ws,
+                     cudaStream_t st) {
+  const int64_t rows = batch * M;
+  const int64_t cap = n_experts + (rows + QMM_SLOT_ROWS - 1) / QMM_SLOT_ROWS;
+  int4* slots = reinterpret_cast<int4*>(ws);
+  bf16* xs = reinterpret_cast<bf16*>(reinterpret_cast<char*>(ws) + (cap * 16 + 255) / 256 * 256);
+  // x already in sorted row order when every batch element reads its own x matrix
+  const bool copy = lhs != nullptr || x_batches != batch;
+  gather_rows_kernel<<<(unsigned)rows, 128, 0, st>>>(x, lhs, x_batches, batch, M, K, rhs, (int)n_experts,
+                                                     copy ? xs : nullptr, y, N);
+  int rc = check_launch("gather_rows_kernel");
+  if (rc) return rc;
+  qmm_slots_kernel<<<1, 1024, 0, st>>>(rhs, batch, M, (int)n_experts, slots, cap);
+  rc = check_launch("qmm_slots_kernel");
+  if (rc) return rc;
+  return launch_qmm_tc_grouped(copy ? xs : x, w, scales, biases, y, rows, N, K, n_experts, slots, cap, bits, gs, st);
+}
+
 }  // namespace vmlx
 
 using namespace vmlx;

@@ -155,7 +155,7 @@ template <int BITS, int GS, int BT, int NH>
 __global__ void __launch_bounds__(TcLayout<BITS, BT, NH>::THREADS, 1)
 qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
               const bf16* __restrict__ scales, const bf16* __restrict__ biases, bf16* __restrict__ y,
-              int M, int N, int K, int S, int* status) {
+              int M, int N, int K, int S, int* status, const int4* __restrict__ slots) {
   using L = TcLayout<BITS, BT, NH>;
   constexpr int SX = L::SX, SA = L::SA, SR = L::SR, TC_BN = L::BN, TC_DQ = L::DQ, TC_WARPS = L::WARPS;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
@@ -175,7 +175,19 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = (int)blockIdx.x % S;
-  const int n0 = ((int)blockIdx.x / S) * TC_BN, m0 = (int)blockIdx.y * BT;
+  const int n0 = ((int)blockIdx.x / S) * TC_BN;
+  // Expert-segmented mode (sorted gather_qmm): blockIdx.y is a slot {expert, first row, rows}
+  // of the expert-sorted x; the tile multiplies those rows by the expert's weights.  Unused
+  // slots (rows == 0) exit before touching any barrier or TMEM (uniform across the cluster,
+  // whose CTAs share blockIdx.y).
+  int m0 = (int)blockIdx.y * BT, m_end = M, wrow0 = 0;
+  if (slots) {
+    const int4 sl = slots[blockIdx.y];
+    if (sl.z <= 0) return;
+    m0 = sl.y;
+    m_end = sl.y + sl.z < M ? sl.y + sl.z : M;
+    wrow0 = sl.x * N;
+  }
   const int KB = K / TC_BK;
   const int kb0 = (int)((int64_t)split * KB / S), nkb = (int)((int64_t)(split + 1) * KB / S) - kb0;
   const int KG = K / GS;
@@ -214,7 +226,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
           const int j = i / L::RKS, sr = j % SR;
           if (j >= SR) ok &= mbar_wait(&r_empty[sr], ((j / SR) - 1) & 1);
           mbar_arrive_expect_tx(&r_full[sr], L::RS);
-          tma_load_2d(raw + (size_t)sr * L::RS, &tmw, kb * L::RAWB, n0, &r_full[sr]);
+          tma_load_2d(raw + (size_t)sr * L::RS, &tmw, kb * L::RAWB, wrow0 + n0, &r_full[sr]);
         }
         if (i >= SX) ok &= mbar_wait(&x_empty[sx], ((i / SX) - 1) & 1);
         mbar_arrive_expect_tx(&x_full[sx], L::XS);
@@ -257,7 +269,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
     const int r = dq & 127;    // row within the half = TMEM lane
     const int q4 = warp & 3;   // this warp's TMEM lane quarter: r == 32*q4 + lane
     const int rt = mh * TC_UM + r;  // row within the tile
-    const int row = n0 + rt < N ? n0 + rt : N - 1;
+    const int row = wrow0 + (n0 + rt < N ? n0 + rt : N - 1);
     const bf16* srow = scales + (int64_t)row * KG;
     const bf16* brow = biases + (int64_t)row * KG;
     // group of this thread's 32 k in stage i (32 k never straddle a group, GS >= 32);
@@ -340,7 +352,7 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
     cg::cluster_group cluster = cg::this_cluster();
     for (int t = t_lo + warp; t < t_hi; t += TC_WARPS) {
       const int m = m0 + t;
-      if (m >= M) break;
+      if (m >= m_end) break;
       float acc[NPL];
 #pragma unroll
       for (int j = 0; j < NPL; j++) acc[j] = 0.f;
@@ -376,7 +388,8 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
 
 template <int BITS, int GS, int BT, int NH>
 static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y, int64_t M,
-                     int64_t N, int64_t K, cudaStream_t st) {
+                     int64_t N, int64_t K, cudaStream_t st, const int4* slots = nullptr, int64_t n_slots = 0,
+                     int64_t n_experts = 1) {
   using L = TcLayout<BITS, BT, NH>;
   auto kern = qmm_tc_kernel<BITS, GS, BT, NH>;
   {
@@ -386,12 +399,12 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
   CUtensorMap tmx, tmw;
   if (!make_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TC_BK,
                     BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K * BITS / 8, (uint64_t)N,
+      !make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K * BITS / 8, (uint64_t)(N * n_experts),
                     (uint64_t)K * BITS / 8, 128, L::BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return VMLX_E_CUDA;
   // K splits fill the SMs when the tile grid is small; each split keeps >= 8 stages, and
   // clusters stay at <= 4 CTAs so that they co-schedule in one wave.
-  const int64_t ntn = (N + L::BN - 1) / L::BN, ntm = (M + BT - 1) / BT;
+  const int64_t ntn = (N + L::BN - 1) / L::BN, ntm = slots ? n_slots : (M + BT - 1) / BT;
   const int64_t tiles = ntn * ntm, KB = K / TC_BK;
   int S = 1;
   while (S < 4 && tiles * S * 2 <= sm_count() && KB / (S * 2) >= 8) S *= 2;
@@ -409,8 +422,9 @@ static int launch_tc(const bf16* x, const uint32_t* w, const bf16* scales, const
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = launch_overlap() ? 2 : 1;
+  if (ntm > 65535) return set_error(VMLX_E_UNSUPPORTED, "qmm_tc: %lld token tiles", (long long)ntm);
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, tmx, tmw, scales, biases, y, (int)M, (int)N, (int)K, S,
-                                       (int*)nullptr),
+                                       (int*)nullptr, slots),
                     "qmm_tc_kernel launch");
 }
 
@@ -447,6 +461,27 @@ int launch_qmm_tc(const bf16* x, const uint32_t* w, const bf16* scales, const bf
   if (bits == 8 && gs == 128) return launch_bt<8, 128>(x, w, scales, biases, y, M, N, K, st);
   *handled = false;
   return VMLX_OK;
+}
+
+// Expert-segmented GEMM for sorted gather_qmm: x [M rows sorted by expert, K], slots
+// {expert, first row, rows} (rows <= 64; unused slots have rows 0), w / scales / biases
+// stacks of n_experts [N, ...] matrices.  One 64-token tile per slot.
+int launch_qmm_tc_grouped(const bf16* x, const uint32_t* w, const bf16* scales, const bf16* biases, bf16* y,
+                          int64_t M, int64_t N, int64_t K, int64_t n_experts, const int4* slots, int64_t n_slots,
+                          int bits, int gs, cudaStream_t st) {
+  if (K % TC_BK || !aligned(x, 16) || !aligned(w, 16) || M >= (1ll << 30) || N * n_experts >= (1ll << 31))
+    return set_error(VMLX_E_UNSUPPORTED, "qmm_tc grouped: shape not covered");
+  const int64_t ntn2 = (N + 255) / 256;
+#define VMLX_GROUPED(B, G)                                                                                   \
+  if (bits == B && gs == G) {                                                                               \
+    if (ntn2 * n_slots >= 112) return launch_tc<B, G, 64, 2>(x, w, scales, biases, y, M, N, K, st, slots, n_slots, \
+                                                             n_experts);                                    \
+    return launch_tc<B, G, 64, 1>(x, w, scales, biases, y, M, N, K, st, slots, n_slots, n_experts);          \
+  }
+  VMLX_GROUPED(4, 32) VMLX_GROUPED(4, 64) VMLX_GROUPED(4, 128) VMLX_GROUPED(8, 32) VMLX_GROUPED(8, 64)
+  VMLX_GROUPED(8, 128)
+#undef VMLX_GROUPED
+  return set_error(VMLX_E_UNSUPPORTED, "qmm_tc grouped: bits=%d group_size=%d", bits, gs);
 }
 
 }  // namespace vmlx

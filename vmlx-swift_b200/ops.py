@@ -159,8 +159,10 @@ def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                         biases: Optional[torch.Tensor], lhs_indices: Optional[torch.Tensor] = None,
                         rhs_indices: Optional[torch.Tensor] = None, transpose: bool = True,
                         group_size: int = 64, bits: int = 4, mode: str = "affine",
-                        sorted_indices: bool = False) -> torch.Tensor:
+                        sorted_indices: bool = False, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """MLX gather_qmm: ``y[i] = x[lhs[i]] @ dequantized(w[rhs[i]])^T`` with broadcasting.
+    workspace (uint8 device tensor of gather_qmm_workspace_size bytes) lets sorted gathers with
+    many rows per expert run on the tensor cores (vmlx_cuda_gather_qmm_ws).
 
     x [*xb, M, K]; w [E, N, K*bits/32]; indices int tensors.  The output shape
     is broadcast(index shapes, xb) + [M, N], as in MLX."""
@@ -193,11 +195,14 @@ def gather_quantized_mm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     lhs32 = lhs.to(torch.int32).contiguous() if lhs is not None else None
     nb = rhs32.numel()
     y = torch.empty(*bshape, M, N, dtype=torch.bfloat16, device=x.device)
-    check(_lib.lib().vmlx_cuda_gather_qmm(
-        y.data_ptr(), x.data_ptr(), w.data_ptr(), scales.data_ptr(),
-        biases.data_ptr() if biases is not None else None,
-        lhs32.data_ptr() if lhs32 is not None else None, rhs32.data_ptr(), transpose, group_size,
-        bits, mode.encode() if mode else None, sorted_indices, nb, x_batches, M, N, K, E, _stream(x)))
+    args = (y.data_ptr(), x.data_ptr(), w.data_ptr(), scales.data_ptr(),
+            biases.data_ptr() if biases is not None else None,
+            lhs32.data_ptr() if lhs32 is not None else None, rhs32.data_ptr(), transpose, group_size,
+            bits, mode.encode() if mode else None, sorted_indices, nb, x_batches, M, N, K, E)
+    if workspace is not None:
+        check(_lib.lib().vmlx_cuda_gather_qmm_ws(*args, workspace.data_ptr(), workspace.numel(), _stream(x)))
+    else:
+        check(_lib.lib().vmlx_cuda_gather_qmm(*args, _stream(x)))
     return y
 
 
@@ -247,3 +252,7 @@ def moe_combine(y: torch.Tensor, scores: torch.Tensor, inverse_order: Optional[t
     check(_lib.lib().vmlx_cuda_moe_combine(yc.data_ptr(), inv.data_ptr() if inv is not None else None, sc.data_ptr(),
                                            _dtype_code(sc.dtype), T, k, D, out.data_ptr(), _stream(yc)))
     return out
+
+
+def gather_qmm_workspace_size(batch: int, M: int, K: int, n_experts: int) -> int:
+    return int(_lib.lib().vmlx_cuda_gather_qmm_workspace_size(batch, M, K, n_experts))

@@ -65,10 +65,20 @@ class QuantizedSwitchLinear:
     def input_dims(self):
         return self.weight.shape[2] * 32 // self.bits
 
+    def _workspace(self, rows: int, k: int, dev):
+        """Workspace of the tensor-core sorted gather, kept and grown per layer."""
+        need = ops.gather_qmm_workspace_size(rows, 1, k, self.num_experts)
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.numel() < need or ws.device != dev:
+            ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            self._ws = ws
+        return ws
+
     def __call__(self, x, indices, sorted_indices: bool = False, lhs: Optional[torch.Tensor] = None):
+        ws = self._workspace(indices.numel(), x.shape[-1], x.device) if sorted_indices else None
         y = ops.gather_quantized_mm(x, self.weight, self.scales, self.biases, lhs_indices=lhs, rhs_indices=indices,
                                     transpose=True, group_size=self.group_size, bits=self.bits,
-                                    mode=self.mode, sorted_indices=sorted_indices)
+                                    mode=self.mode, sorted_indices=sorted_indices, workspace=ws)
         if self.bias is not None:
             y = y + self.bias[indices].unsqueeze(-2)
         return y
