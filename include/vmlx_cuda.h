@@ -312,6 +312,19 @@ VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, v
  * pass peer buffers (vmlx_tp_buffer of the other handles) to vmlx_tp_set_peer.
  */
 VMLX_API int vmlx_tp_create(int rank, int world, size_t max_bytes, void** out);
+/*
+ * A whole group of `world` ranks (2..8) on the current device, run as one grid per
+ * call: the single-GPU form of the group, for testing the collective protocol
+ * (the same kernels, word formats, epochs and rank-order sums as a group with one
+ * GPU per rank) and for hosts with fewer GPUs than ranks.  No reference
+ * counterpart (the reference has one process per rank).  On such a handle every
+ * data pointer of vmlx_tp_all_sum / vmlx_tp_quantized_matmul_*_all_sum holds all
+ * ranks' data stacked along a leading rank axis: in / out [world, n]; x [world, M, K]
+ * (gate_up [world, M, 2K]); y and residual [world, M, N]; w / scales / biases the
+ * ranks' shards stacked along N ([world * N, ...]).  Each call is one cooperative
+ * launch (all ranks' CTAs resident together, else the call fails).
+ */
+VMLX_API int vmlx_tp_create_loopback(int world, size_t max_bytes, void** out);
 VMLX_API int vmlx_tp_rank(void* tp);
 VMLX_API int vmlx_tp_size(void* tp);
 VMLX_API int vmlx_tp_ipc_handle(void* tp, void* handle_out);
@@ -343,8 +356,10 @@ VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, voi
  * plus the decoder residual add (Libraries/MLXLLM/Models/Llama.swift:110-114).
  * One kernel per rank: the GEMV pushes its bf16 partial rows into every rank's
  * slot over NVLink P2P as 8-byte {value, epoch} words; each CTA then polls
- * (bounded) the words of the rows it computed and sums them in rank order -- bitwise equal to quantized_matmul,
- * vmlx_tp_all_sum and add run separately.  residual may be NULL or alias y.
+ * (bounded) the words of the rows it computed and sums them in rank order, so y has the same bits on
+ * every rank.  The partial rows come from the 1-32-row GEMV kernel's TP instance; the separate
+ * quantized_matmul -> vmlx_tp_all_sum -> add chain may pick another GEMV kernel for the partials and
+ * then agrees within the GEMV tolerance, not bitwise.  residual may be NULL or alias y.
  * Every rank must make the same sequence of calls.  Size 1: the local fused GEMV.
  */
 VMLX_API int vmlx_tp_quantized_matmul_all_sum(void* tp, void* y, const void* x, const uint32_t* w,

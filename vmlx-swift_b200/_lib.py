@@ -65,6 +65,7 @@ SIGNATURES = {
     "vmlx_cuda_silu_mul": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
     "vmlx_tp_create": (_int, [_int, _int, _sz, _c.POINTER(_vp)]),
+    "vmlx_tp_create_loopback": (_int, [_int, _sz, _c.POINTER(_vp)]),
     "vmlx_tp_rank": (_int, [_vp]),
     "vmlx_tp_size": (_int, [_vp]),
     "vmlx_tp_ipc_handle": (_int, [_vp, _vp]),

@@ -44,6 +44,11 @@ struct QmvArgs {
   size_t tp_slots_off, tp_flags_off, tp_epoch_off;  // regions inside each buffer
   uint64_t tp_timeout_ns;
   int* tp_status;  // set to VMLX_E_PEER_TIMEOUT when a peer wait runs out
+  // Loopback group (tp_loop = 1): every rank of the group lives on this device and the
+  // ranks run as one grid, rank = blockIdx.y.  x / y / residual hold all ranks' rows
+  // stacked along a leading rank axis ([world, M, .]) and the weights all ranks' shards
+  // stacked along N ([world * N, .]).
+  int tp_loop;
 };
 
 constexpr int TP_FUSED_MAXC = 1024;  // CTAs of a fused TP GEMV grid (flag slots per rank)

@@ -75,6 +75,7 @@ __device__ __forceinline__ int64_t lower_bound_u32(const uint32_t* a, int64_t n,
 __device__ __forceinline__ void token_rows(const QmvArgs& p, int mode, int64_t b_or_r0, int64_t tok,
                                            const bf16*& xr, bf16*& yr) {
   if (mode == QMV_DENSE) {
+    tok += b_or_r0;  // 0, or a loopback rank's first row
     xr = p.x + tok * (p.x_swiglu ? 2 * p.K : p.K);
     yr = p.y + tok * p.N;
   } else if (mode == QMV_GATHER) {
@@ -106,12 +107,14 @@ __device__ __forceinline__ void unpack4(uint32_t w, uint32_t (&p)[4]) {
 // Store one output element, with the optional fused residual add.  Under row-parallel
 // TP the bf16 partial goes to slot [parity][tp_rank] of every rank instead, as one
 // low-latency word {bf16 bits, epoch} per element (P2P 8-byte stores).
+// (trank: this CTA's rank; ybias: offset of that rank's rows in a loopback group's y).
 template <bool TP>
-__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v, uint32_t tp_e) {
+__device__ __forceinline__ void store_y(const QmvArgs& p, bf16* yr, int64_t col, float v, uint32_t tp_e,
+                                        int trank, int64_t ybias) {
   if constexpr (TP) {
     const uint32_t hv = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
-    const size_t off = p.tp_slots_off + ((size_t)(tp_e & 1) * p.tp_world + p.tp_rank) * p.tp_slot_bytes +
-                       (size_t)((yr - p.y) + col) * sizeof(uint64_t);
+    const size_t off = p.tp_slots_off + ((size_t)(tp_e & 1) * p.tp_world + trank) * p.tp_slot_bytes +
+                       (size_t)((yr - p.y) - ybias + col) * sizeof(uint64_t);
     for (int r = 0; r < p.tp_world; r++) st_ll(reinterpret_cast<uint64_t*>(p.tp_buf[r] + off), hv, tp_e);
     return;
   }
@@ -156,13 +159,14 @@ struct QmvItem {
   bool zero_rows;
 };
 
-__device__ __forceinline__ QmvItem qmv_item(const QmvArgs& p, int mode, int64_t item, int64_t rowtiles) {
+// lr: a loopback rank (0 otherwise), whose rows and weight shard the dense item uses.
+__device__ __forceinline__ QmvItem qmv_item(const QmvArgs& p, int mode, int64_t item, int64_t rowtiles, int lr = 0) {
   QmvItem it;
   const int64_t z = item / rowtiles;
   it.n0 = (item - z * rowtiles) * QMV_ROWS;
-  it.base = 0;
+  it.base = (int64_t)lr * p.M;
   it.ntok = p.M;
-  it.e = 0;
+  it.e = lr;
   it.zero_rows = false;
   if (mode == QMV_GATHER) {
     it.base = z;
@@ -202,6 +206,11 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   const int XST = TOKA * 32 + 4;    // fp32 x stride per chunk (CUDA-core path), padded
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // TP ranks: trank = this CTA's rank in the group; lr = the same for a loopback group
+  // (all ranks in one grid, rank = blockIdx.y), else 0.
+  const int lr = (TP && p.tp_loop) ? (int)blockIdx.y : 0;
+  const int trank = TP ? (p.tp_loop ? lr : p.tp_rank) : 0;
+  const int64_t ybias = (int64_t)lr * p.M * p.N;
   const int rank = (int)(blockIdx.x % C);  // K-slice == rank in the cluster (cluster dims (C,1,1))
   const int64_t cluster_id = blockIdx.x / C, n_clusters = gridDim.x / C;
   const int64_t KG = p.K / GS;
@@ -262,7 +271,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     if (mode != QMV_DENSE) asm volatile("griddepcontrol.wait;" ::: "memory");
     bool pend = false;
     for (int64_t item = it_lo; item < it_hi; item += it_step) {
-      const QmvItem I = qmv_item(p, mode, item, rowtiles);
+      const QmvItem I = qmv_item(p, mode, item, rowtiles, lr);
       if (I.ntok == 0) continue;
       const int ybase = (int)(I.e * p.N + I.n0);  // row coordinate in the [E*N, .] maps
       if (!I.zero_rows) {
@@ -313,13 +322,13 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
     // Row-parallel TP: this call's epoch (advanced by the grid's last CTA) picks the slot parity.
     __shared__ uint32_t s_tp_e;
     if constexpr (TP) {
-      if (tid == 0) s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off) + 1;
+      if (tid == 0) s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[trank] + p.tp_epoch_off) + 1;
       named_bar_sync(1, 32 * QMV_CWARPS);
     }
     const uint32_t tp_e = TP ? s_tp_e : 0u;
     int64_t staged_z = -1;  // token set (item / rowtiles) whose x is staged
     for (int64_t item = it_lo; item < it_hi; item += it_step) {
-      const QmvItem I = qmv_item(p, mode, item, rowtiles);
+      const QmvItem I = qmv_item(p, mode, item, rowtiles, lr);
       if (I.ntok == 0) continue;
       int slot_sc = 0;
       if (!I.zero_rows) {
@@ -551,7 +560,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                 const bf16* xr_unused;
                 bf16* yr;
                 token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-                store_y<TP>(p, yr, row, acc[t][j], tp_e);
+                store_y<TP>(p, yr, row, acc[t][j], tp_e, trank, ybias);
               }
             }
           }
@@ -660,7 +669,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
                     const bf16* xr_unused;
                     bf16* yr;
                     token_rows(p, mode, I.base, chunk + t, xr_unused, yr);
-                    store_y<TP>(p, yr, I.n0 + r, res[j][t], tp_e);
+                    store_y<TP>(p, yr, I.n0 + r, res[j][t], tp_e, trank, ybias);
                   }
                 } else {
                   rb[r * TOKA + t] = res[j][t];
@@ -681,7 +690,7 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
               const bf16* xr_unused;
               bf16* yr;
               token_rows(p, mode, I.base, chunk + tok, xr_unused, yr);
-              store_y<TP>(p, yr, I.n0 + r, s, tp_e);
+              store_y<TP>(p, yr, I.n0 + r, s, tp_e, trank, ybias);
             }
           }
           red_count++;
@@ -697,12 +706,12 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
       // (each word is polled until it carries this call's epoch: no separate flags or fences)
       const uint64_t deadline = globaltimer() + p.tp_timeout_ns;
       const int rlo = C > 1 ? crow_lo : 0, rhi = C > 1 ? crow_hi : QMV_ROWS, nr = rhi - rlo;
-      const uint64_t* slots = reinterpret_cast<const uint64_t*>(p.tp_buf[p.tp_rank] + p.tp_slots_off +
+      const uint64_t* slots = reinterpret_cast<const uint64_t*>(p.tp_buf[trank] + p.tp_slots_off +
                                                                 (size_t)(tp_e & 1) * p.tp_world * p.tp_slot_bytes);
       const size_t rstride = p.tp_slot_bytes / sizeof(uint64_t);
       bool tp_ok = true;
       for (int64_t item = cluster_id; item < n_items && tp_ok; item += n_clusters) {
-        const QmvItem I = qmv_item(p, mode, item, rowtiles);
+        const QmvItem I = qmv_item(p, mode, item, rowtiles, lr);
         for (int64_t i = tid; i < (int64_t)nr * I.ntok && tp_ok; i += 32 * QMV_CWARPS) {
           const int64_t row = I.n0 + rlo + i % nr, tok = i / nr;
           if (row >= p.N) continue;
@@ -711,13 +720,14 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
           tp_ok = wait_ll_sum<QMV_TP_MAX_WORLD>(slots + idx, rstride, p.tp_world, tp_e, deadline, sum);
           if (!tp_ok) break;
           const bf16 sb = __float2bfloat16_rn(sum);
-          p.y[idx] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + __bfloat162float(sb)) : sb;
+          const int64_t yi = idx + ybias;
+          p.y[yi] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[yi]) + __bfloat162float(sb)) : sb;
         }
       }
       if (!tp_ok && p.tp_status) atomicExch(p.tp_status, VMLX_E_PEER_TIMEOUT);
       named_bar_sync(1, 32 * QMV_CWARPS);
       if (tid == 0) {  // the grid's last CTA advances the epoch for the next call
-        uint32_t* ep = reinterpret_cast<uint32_t*>(p.tp_buf[p.tp_rank] + p.tp_epoch_off);
+        uint32_t* ep = reinterpret_cast<uint32_t*>(p.tp_buf[trank] + p.tp_epoch_off);
         __threadfence();
         if (atomicAdd(ep + 1, 1u) == gridDim.x - 1) {
           ep[1] = 0;
@@ -743,7 +753,7 @@ static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
     const int rc = ensure_max_dynamic_smem((const void*)kern, 226 * 1024);  // + static smem <= 227 KB
     if (rc) return rc;
   }
-  const int64_t E = (mode == QMV_DENSE) ? 1 : a.n_experts;
+  const int64_t E = (mode == QMV_DENSE) ? (a.tp_loop ? a.tp_world : 1) : a.n_experts;
   const int64_t KG = a.K / GS;
   CUtensorMap tmw, tms, tmb;
   if (!make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)a.K * BITS / 8, (uint64_t)(E * a.N),
@@ -766,15 +776,37 @@ static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, QMV_THREADS, L.total);
   if (e != cudaSuccess || per_sm < 1) per_sm = 1;
   if (per_sm > QMV_MAX_PER_SM) per_sm = QMV_MAX_PER_SM;
-  int64_t max_clusters = (int64_t)sm_count() * per_sm / C;
+  // A loopback group runs every rank's grid in one launch: the ranks share the SMs.
+  const int ranks = (TP && a.tp_loop) ? a.tp_world : 1;
+  int64_t max_clusters = (int64_t)sm_count() * per_sm / C / ranks;
   if (max_clusters < 1) max_clusters = 1;
+  if (ranks > 1) {  // clusters of C CTAs that can be resident at once, shared by the ranks
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3((unsigned)C, 1, 1);
+    q.blockDim = dim3(QMV_THREADS);
+    q.dynamicSmemBytes = L.total;
+    cudaLaunchAttribute ca;
+    ca.id = cudaLaunchAttributeClusterDimension;
+    ca.val.clusterDim.x = (unsigned)C;
+    ca.val.clusterDim.y = 1;
+    ca.val.clusterDim.z = 1;
+    q.attrs = &ca;
+    q.numAttrs = 1;
+    int resident = 0;
+    if (cudaOccupancyMaxActiveClusters(&resident, kern, &q) != cudaSuccess || resident < ranks) {
+      cudaGetLastError();
+      return set_error(VMLX_E_UNSUPPORTED, "tp loopback: %d ranks of %d-CTA clusters cannot be resident together",
+                       ranks, C);
+    }
+    if (max_clusters > resident / ranks) max_clusters = resident / ranks;
+  }
   const int64_t n_clusters = n_items < max_clusters ? n_items : max_clusters;
 
   if (a.tp_world > 1 && n_clusters * C > TP_FUSED_MAXC)
     return set_error(VMLX_E_UNSUPPORTED, "tp: fused grid of %lld CTAs exceeds %d", (long long)(n_clusters * C),
                      TP_FUSED_MAXC);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(n_clusters * C), 1, 1);
+  cfg.gridDim = dim3((unsigned)(n_clusters * C), (unsigned)ranks, 1);
   cfg.blockDim = dim3(QMV_THREADS);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
@@ -787,6 +819,13 @@ static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = launch_overlap() ? 2 : 1;
+  if (ranks > 1) {
+    // The ranks' CTAs wait on one another: a cooperative launch guarantees that the whole
+    // grid is resident at once (or refuses the launch).  No programmatic overlap.
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.numAttrs = 2;
+  }
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, a, tmw, tms, tmb, sc_tma, mode, ks, C, toka, rowtiles, n_items),
                     "qmv_kernel launch");
 }

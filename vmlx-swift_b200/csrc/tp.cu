@@ -52,6 +52,7 @@ struct TpHandle {
   int* status;             // device word: 0 or VMLX_E_PEER_TIMEOUT
   uint64_t timeout_ns;
   bool connected;
+  bool loop;               // loopback group: every rank's buffer on this device, ranks run as one grid
 };
 
 __host__ __device__ inline size_t tp_slot_off(int parity, int src, size_t max_bytes, int world) {
@@ -99,7 +100,12 @@ __device__ __forceinline__ void tp_advance_epoch(uint32_t* epoch_p, uint32_t e) 
 // One-shot all-reduce of n bf16 elements (n * 2 <= max_bytes, chunked over CTAs).
 __global__ void __launch_bounds__(TP_THREADS)
 tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
-                  bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns) {
+                  bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns, int loop) {
+  if (loop) {  // loopback group: rank = blockIdx.y, in / out stacked [world, n]
+    rank = blockIdx.y;
+    in += (int64_t)rank * n;
+    out += (int64_t)rank * n;
+  }
   const int c = blockIdx.x;
   const int64_t e0 = (int64_t)c * chunk;
   const int64_t e1 = e0 + chunk < n ? e0 + chunk : n;
@@ -164,7 +170,12 @@ tp_all_sum_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf
 // same rank-order fp32 sum.
 __global__ void __launch_bounds__(TP_THREADS)
 tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ in,
-                     bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns) {
+                     bf16* __restrict__ out, int64_t n, int64_t chunk, int* status, uint64_t timeout_ns, int loop) {
+  if (loop) {
+    rank = blockIdx.y;
+    in += (int64_t)rank * n;
+    out += (int64_t)rank * n;
+  }
   const int c = blockIdx.x;
   const int64_t e0 = (int64_t)c * chunk;
   const int64_t e1 = e0 + chunk < n ? e0 + chunk : n;
@@ -231,6 +242,38 @@ extern "C" int vmlx_tp_create(int rank, int world, size_t max_bytes, void** out)
     return rc;
   }
   h->peer_base[rank] = h->local;
+  *out = h;
+  return VMLX_OK;
+}
+
+extern "C" int vmlx_tp_create_loopback(int world, size_t max_bytes, void** out) {
+  if (!out) return set_error(VMLX_E_INVALID, "tp_create_loopback: null out");
+  if (world < 2 || world > TP_MAX_WORLD)
+    return set_error(VMLX_E_INVALID, "tp_create_loopback: world %d (2..%d)", world, TP_MAX_WORLD);
+  if (max_bytes == 0 || max_bytes % 16)
+    return set_error(VMLX_E_INVALID, "tp_create_loopback: max_bytes must be a positive multiple of 16");
+  TpHandle* h = new TpHandle();
+  std::memset(h, 0, sizeof(*h));
+  h->rank = 0;
+  h->world = world;
+  h->max_bytes = max_bytes;
+  h->timeout_ns = 2000000000ull;
+  h->loop = true;
+  int rc = check_cuda(cudaGetDevice(&h->device), "tp_create_loopback: cudaGetDevice");
+  h->total_bytes = tp_total_bytes(max_bytes, world);
+  const size_t stride = (h->total_bytes + 255) / 256 * 256;
+  if (!rc) rc = check_cuda(cudaMalloc(&h->local, stride * world), "tp_create_loopback: cudaMalloc");
+  if (!rc) rc = check_cuda(cudaMemset(h->local, 0, stride * world), "tp_create_loopback: cudaMemset");
+  if (!rc) rc = check_cuda(cudaMalloc(&h->status, sizeof(int)), "tp_create_loopback: cudaMalloc status");
+  if (!rc) rc = check_cuda(cudaMemset(h->status, 0, sizeof(int)), "tp_create_loopback: cudaMemset status");
+  if (rc) {
+    if (h->local) cudaFree(h->local);
+    if (h->status) cudaFree(h->status);
+    delete h;
+    return rc;
+  }
+  for (int r = 0; r < world; r++) h->peer_base[r] = h->local + (size_t)r * stride;
+  h->connected = true;
   *out = h;
   return VMLX_OK;
 }
@@ -318,12 +361,25 @@ extern "C" int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, v
     if (ctas > TP_MAX_CTAS) ctas = TP_MAX_CTAS;
     chunk = (n + ctas - 1) / ctas;
     ctas = (n + chunk - 1) / chunk;
-    tp_all_sum_ll_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
-        peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
-  } else
-    tp_all_sum_kernel<<<(unsigned)ctas, TP_THREADS, 0, as_stream(stream)>>>(
-        peers, h->rank, h->world, h->max_bytes, (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns);
-  return check_launch("tp_all_sum_kernel");
+  }
+  const bool ll = (size_t)n * 8 <= h->max_bytes;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas, h->loop ? (unsigned)h->world : 1u, 1);
+  cfg.blockDim = dim3(TP_THREADS);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr;
+  if (h->loop) {  // the ranks' CTAs wait on one another: all resident at once, or no launch
+    attr.id = cudaLaunchAttributeCooperative;
+    attr.val.cooperative = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+  }
+  const int rank = h->loop ? 0 : h->rank, loop = h->loop ? 1 : 0;
+  return check_cuda(ll ? cudaLaunchKernelEx(&cfg, tp_all_sum_ll_kernel, peers, rank, h->world, h->max_bytes,
+                                            (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns, loop)
+                       : cudaLaunchKernelEx(&cfg, tp_all_sum_kernel, peers, rank, h->world, h->max_bytes,
+                                            (const bf16*)in, (bf16*)out, n, chunk, h->status, h->timeout_ns, loop),
+                    "tp_all_sum_kernel launch");
 }
 
 // Row-parallel quantized linear fused with its all-reduce (and the residual add):
@@ -378,7 +434,7 @@ static int tp_qmm_all_sum(void* tp, void* y, const void* x, const uint32_t* w, c
   QmvArgs a{(const bf16*)x, w, (const bf16*)scales, (const bf16*)biases, (bf16*)y, nullptr, nullptr,
             M, N, K, 0, 1, 1, nullptr, nullptr, 0.f, (const bf16*)residual};
   for (int r = 0; r < TP_MAX_WORLD; r++) a.tp_buf[r] = r < h->world ? h->peer_base[r] : nullptr;
-  a.tp_rank = h->rank;
+  a.tp_rank = h->loop ? 0 : h->rank;
   a.tp_world = h->world;
   a.tp_slot_bytes = h->max_bytes;
   a.tp_slots_off = tp_fused_slots_off(h->max_bytes, h->world);
@@ -387,6 +443,7 @@ static int tp_qmm_all_sum(void* tp, void* y, const void* x, const uint32_t* w, c
   a.tp_timeout_ns = h->timeout_ns;
   a.tp_status = h->status;
   a.x_swiglu = swiglu;
+  a.tp_loop = h->loop ? 1 : 0;
   if (swiglu && K % 8) return set_error(VMLX_E_INVALID, "tp: SwiGLU input needs K a multiple of 8");
   return launch_qmv(a, QMV_DENSE, bits, group_size, 1, (int)M, as_stream(stream));
 }
