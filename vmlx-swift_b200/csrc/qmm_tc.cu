@@ -38,54 +38,7 @@ namespace cg = cooperative_groups;
 namespace vmlx {
 
 
-constexpr int TC_UM = 128;  // UMMA M (weight rows per MMA = TMEM lanes)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row of bf16)
-
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  // start address >> 4 | LBO (unused for swizzled K-major, 1) | SBO = 1024 B between
-  // 8-row groups | descriptor version 1 | layout SWIZZLE_128B
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128.
-__host__ __device__ constexpr uint32_t tc_idesc(int bt) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bt >> 3) << 17) | ((uint32_t)(TC_UM >> 4) << 24);
-}
-
-// A from tensor memory (row = lane, K-major, two bf16 per column), B from shared memory.
-__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
-                                            uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 8 4-bit codes (one packed word, LSB first) -> 8 bf16 s*q + b, each rounded once.
 // Codes are made exact as bf16 128+q (high byte 0x43, q in the low mantissa bits).
@@ -294,6 +247,9 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ C
         wv[4 * v] = u.x; wv[4 * v + 1] = u.y; wv[4 * v + 2] = u.z; wv[4 * v + 3] = u.w;
       }
       if (sub == L::RKS - 1 || i == nkb - 1) {
+        // the codes must be in registers before the stage is released to the next TMA
+#pragma unroll
+        for (int v = 0; v < BITS; v++) asm volatile("" ::"r"(wv[v]));
         __syncwarp();
         if (lane == 0) mbar_arrive(&r_empty[sr]);
       }
