@@ -197,9 +197,9 @@ def bench_gemv(args, torch, vm, dev):
                     t = time_graph_calls(torch, cl, 8, 3, stream)
                     gbs = gemv_bytes(MM, NN, KK, b, 64) / t / 1e9
                     row = {"us": round(t * 1e6, 2), "GBps": round(gbs, 1), "frac_8TBps": round(gbs / 8000, 3),
-                           "kernel": "qmv_kernel (GEMV, CUDA cores / mma.sync)" if MM <= 32 else
-                                     "qmm_tc_kernel (tcgen05, TMEM)"}
-                    if MM > 32:  # tensor-core regime: the tensor roofline
+                           "kernel": ("qgemv_kernel / qmv_kernel (CUDA cores)" if MM <= 4 else
+                                      "qmm_tc_kernel (tcgen05, TMEM)")}
+                    if MM > 4:  # tensor-core regime: the tensor roofline as well
                         tfs = 2.0 * MM * NN * KK / t / 1e12
                         row.update({"TFLOPs": round(tfs, 1), "frac_of_bf16_peak": round(tfs / tf, 4)})
                     sweep[f"K{KK}_N{NN}_b{b}_M{MM}"] = row
@@ -499,7 +499,7 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
                    "graph": "whole decode step captured in one CUDA graph", "launch_overlap": "on"},
         "step_hbm": {"bytes_per_rank": nbytes, "GBps_per_rank": round(nbytes / t_step / 1e9, 1),
                      "frac_of_measured": round(nbytes / t_step / 1e9 / hbm, 4)},
-        "roofline": {"bound": "hbm", "kernel": "qmv_kernel (decode GEMV)", "achieved": round(gemv_achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "decode GEMVs (qgemv_kernel up to 8K x 8K, qmv_kernel above)", "achieved": round(gemv_achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(gemv_achieved / hbm, 4), "peak_source": peak_src,
                      "frac_of_8TBps": round(gemv_achieved / 8000, 4),
                      "traffic": load_traffic(f"qmv_decode_B{B}_tp{world}"),
@@ -520,6 +520,91 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
             torch.cuda.synchronize()
             torch.cuda.nvtx.range_pop()
     return res
+
+
+def bench_qwen3(args, torch, vm, dev):
+    """Qwen3-32B-shaped greedy generation (64 layers, 4-bit g64, vocab 151936).
+    The prompt (args.ctx token ids, uniform over the vocabulary) is prefilled untimed; a step is
+    one generated token per sequence: embedding, 64 blocks, lm_head, argmax, all in one CUDA graph
+    that reads and advances the position on the device."""
+    hbm, tf, tf_s, peak_src = peaks()
+    cfg = vm.qwen3.Qwen3Config(n_layers=args.layers if args.layers != 32 else 64)
+    B, T = args.batch, args.ctx if args.ctx != 4096 else 2048
+    vm.lib().vmlx_set_launch_overlap(1)
+    n_e2e = max(8, args.steps // 2)
+    max_len = T + max(3, args.warmup) + args.steps + n_e2e + 8  # every replayed step appends one position
+    dec = vm.qwen3.Qwen3Decoder(cfg, B, max_len=max_len, dev=dev, seed=0)
+    prompt = torch.randint(0, cfg.vocab, (B, T), device=dev, generator=torch.Generator(device=dev).manual_seed(1))
+    t0 = time.perf_counter()
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    t_prefill = time.perf_counter() - t0
+    stream = torch.cuda.Stream(dev)
+    g = dec.capture(stream)
+    clk = ClockSampler(dev.index or 0).__enter__()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        stream.synchronize()
+        ev[0].record(stream)
+        for i in range(args.steps):
+            g.replay()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    per_step = [ev[i].elapsed_time(ev[i + 1]) / 1e3 for i in range(args.steps)]
+    t_step = statistics.median(per_step)
+    ctx_mid = T + max(3, args.warmup) + args.steps // 2
+    kv_bytes = cfg.n_layers * B * cfg.n_kv_heads * ctx_mid * cfg.head_dim * 2 * 2
+    nbytes = dec.weight_bytes + kv_bytes
+    # dominant kernels: the step's quantized GEMVs (4 per block + lm_head), timed alone in a graph
+    x = torch.randn(B, cfg.hidden, device=dev).bfloat16()
+    calls = []
+    for L in dec.layers:
+        calls += [lambda L=L: L.qkv(x, out=dec.qkv_buf), lambda L=L: L.o(dec.attn.view(B, -1), out=dec.proj),
+                  lambda L=L: L.gate_up(x, out=dec.gu), lambda L=L: L.down(dec.act, out=dec.proj)]
+    calls.append(lambda: dec.lm_head(x, out=dec.logits))
+    t_gemv = time_graph_calls(torch, calls, 3, 2, stream)
+    gemv_bytes = sum(l.nbytes for l in dec.layers) + dec.lm_head.nbytes
+    gemv_bytes_avg = gemv_bytes / len(calls)
+    clk.__exit__(None, None, None)
+    # end to end: the sampled ids to the host and the next step's ids from the host, every step
+    ids_h = torch.empty(B, dtype=torch.int32).pin_memory()
+    ids_h.copy_(dec.ids.cpu())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(n_e2e):
+            dec.ids.copy_(ids_h, non_blocking=True)
+            g.replay()
+            ids_h.copy_(dec.ids, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = e0.elapsed_time(e1) / 1e3 / n_e2e
+    return {
+        "metric": "decode tokens/s (Qwen3-32B-shaped greedy generation, 4-bit g64)",
+        "value": round(B / t_step, 2), "unit": "tokens/s", "higher_is_better": True,
+        "ms_per_step": t_step * 1e3, "step_statistic": "median", "dtype": "bf16",
+        "config": {"workload": f"BASELINE config 5: {cfg.n_layers} Qwen3-32B-shaped blocks (hidden 5120, 64 Q / 8 "
+                               f"KV heads, hd 128, FFN 25600, vocab 151936, 4-bit g64), batch {B}, prompt {T} "
+                               f"uniform ids prefilled untimed, greedy decode steps, TP=1",
+                   "batch": B, "prompt": T, "layers": cfg.n_layers, "parallelism": "tp1",
+                   "prefill_s": round(t_prefill, 2),
+                   "l2": f"inputs larger than L2: {nbytes / 1e9:.2f} GB of weights + KV per step",
+                   "graph": "one CUDA graph per token (device-side position), replayed", "launch_overlap": "on"},
+        "step_hbm": {"bytes": nbytes, "GBps": round(nbytes / t_step / 1e9, 1),
+                     "frac_of_measured": round(nbytes / t_step / 1e9 / hbm, 4)},
+        "roofline": {"bound": "hbm", "kernel": "decode GEMVs (qgemv_kernel / qmv_kernel) incl. lm_head",
+                     "achieved": round(gemv_bytes_avg / t_gemv / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gemv_bytes_avg / t_gemv / 1e9 / hbm, 4), "peak_source": peak_src,
+                     "traffic": None, "algorithmic_bytes_per_launch": int(gemv_bytes_avg),
+                     "us_per_launch": round(t_gemv * 1e6, 2)},
+        "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
+                "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
+        "gpu_launches": args.steps * dec.launches_per_step,
+        "status": int(dec.status.item()),
+        "clocks": clk.summary(),
+    }
 
 
 def cpu_baseline_decode(B, ctx, cfg, seconds=10.0):
@@ -568,7 +653,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=os.environ.get("VMLX_BENCH_WORKLOAD", "decode"),
-                    choices=["gemv", "decode", "moe"])
+                    choices=["gemv", "decode", "moe", "qwen3"])
     ap.add_argument("--quick", action="store_true", help="skip the config-2 sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -599,6 +684,14 @@ def main():
                     "vs_baseline": None, "data": "synthetic (seeded random experts, router logits and tokens)"})
         if rank == 0:
             print(json.dumps(res), flush=True)
+        return
+    if args.workload == "qwen3":
+        if world > 1:
+            raise SystemExit("the qwen3 workload runs at TP=1 (the tensor-parallel path is the decode workload)")
+        res = bench_qwen3(args, torch, vm, dev)
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
+                    "vs_baseline": None, "data": "synthetic (seeded random-init quantized weights and prompt ids)"})
+        print(json.dumps(res), flush=True)
         return
     if args.workload == "gemv":
         if world > 1:

@@ -296,6 +296,53 @@ VMLX_API int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, in
 /* out = bf16(a + b), n elements (the residual adds of a decoder block). */
 VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream);
 
+/* ---- the decode loop around the linears (one CUDA graph per token) ---- */
+
+/*
+ * Quantized embedding lookup: out[i, :] = dequantize(w[ids[i]], scales[ids[i]], biases[ids[i]])
+ * (bf16 arithmetic of affine_dequantize), i < n.  Replaces QuantizedEmbedding.callAsFunction
+ * (Source/MLXNN/Quantized.swift:229-236).  w [vocab, dims*bits/32] u32, scales / biases bf16
+ * [vocab, dims/group_size].  An id outside [0, vocab) gives a zero row and sets *status (when
+ * given) to VMLX_E_INVALID.
+ */
+VMLX_API int vmlx_cuda_quantized_embedding(void* out, const int32_t* ids, const uint32_t* w, const void* scales,
+                                           const void* biases, int group_size, int bits, int64_t n, int64_t vocab,
+                                           int64_t dims, int* status, void* stream);
+
+/*
+ * RoPE (non-traditional, pairs (i, i + D/2)) of the q and k heads of qkv [rows, (Hq + 2*Hkv) * D],
+ * each head first RMS-normalised over D with q_norm / k_norm [D] when given (Qwen3Attention's
+ * qNorm / kNorm, Libraries/MLXLLM/Models/Qwen3.swift:75-80; NULL skips the norm), then q to
+ * q_out [rows, Hq, D] and k, v appended to the caches [seqs, Hkv, max_len, D]
+ * (KVCacheSimple.update, Libraries/MLXLMCommon/KVCache.swift:452-470).  The base position is
+ * *pos_dev when pos_dev is not NULL (read on the device: one captured graph serves every
+ * step), else pos.  tokens_per_seq = 0: row r is sequence r at the base position (decode);
+ * T > 0: row r is token r % T of sequence r / T at base + r % T (prefill of T tokens per sequence).  head_dim 64, 128 or 256.  A position
+ * outside the cache skips the row and sets *status (when given) to VMLX_E_INVALID.
+ */
+VMLX_API int vmlx_cuda_rope_qk_norm(void* q_out, void* k_cache, void* v_cache, const void* qkv, int64_t rows,
+                                    int n_heads, int n_kv_heads, int head_dim, const int32_t* pos_dev, int64_t pos,
+                                    int tokens_per_seq, int64_t max_len, const void* q_norm, const void* k_norm,
+                                    float eps, float base, float scale, int* status, void* stream);
+
+/*
+ * vmlx_cuda_sdpa_decode with the cache length read on the device: kv_len = *pos_dev + 1.  The
+ * workspace is sized for max_len (vmlx_cuda_sdpa_decode_workspace(batch, n_heads, max_len, 128)).
+ */
+VMLX_API int vmlx_cuda_sdpa_decode_at(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                      int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                      const int32_t* pos_dev, int64_t max_len, float scale, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
+/*
+ * Greedy sampling: out[r] = the first index of the maximum of logits[r, :vocab] (bf16), the
+ * ArgMaxSampler of Libraries/MLXLMCommon/Evaluate.swift:515-521.
+ */
+VMLX_API int vmlx_cuda_argmax(int32_t* out, const void* logits, int64_t rows, int64_t vocab, void* stream);
+
+/* *counter += delta on the device (the token loop's position, advanced inside the graph). */
+VMLX_API int vmlx_cuda_advance(int32_t* counter, int32_t delta, void* stream);
+
 /* ---- tensor parallelism (one rank per GPU) ---- */
 
 /*

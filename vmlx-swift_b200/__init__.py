@@ -12,5 +12,5 @@ from .nn import QuantizedLinear  # noqa: F401
 from .switch_layers import (QuantizedSwitchLinear, SwitchGLU, Qwen3MoESparseMoeBlock, gather_sort,  # noqa: F401
                             scatter_unsort)
 from .ops import moe_combine, moe_route, moe_sort  # noqa: F401
-from . import fast, llama  # noqa: F401,E402
+from . import fast, llama, qwen3  # noqa: F401,E402
 from . import distributed  # noqa: F401,E402

@@ -64,6 +64,13 @@ SIGNATURES = {
                                              _c.c_float, _vp]),
     "vmlx_cuda_silu_mul": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "vmlx_cuda_quantized_embedding": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64, _vp, _vp]),
+    "vmlx_cuda_rope_qk_norm": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _i64, _int, _i64, _vp, _vp,
+                                      _c.c_float, _c.c_float, _c.c_float, _vp, _vp]),
+    "vmlx_cuda_sdpa_decode_at": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _i64, _c.c_float, _vp, _sz,
+                                        _vp]),
+    "vmlx_cuda_argmax": (_int, [_vp, _vp, _i64, _i64, _vp]),
+    "vmlx_cuda_advance": (_int, [_vp, _c.c_int32, _vp]),
     "vmlx_tp_create": (_int, [_int, _int, _sz, _c.POINTER(_vp)]),
     "vmlx_tp_create_loopback": (_int, [_int, _sz, _c.POINTER(_vp)]),
     "vmlx_tp_rank": (_int, [_vp]),

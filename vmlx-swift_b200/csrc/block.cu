@@ -135,7 +135,8 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
 __global__ void __launch_bounds__(SDPA_THREADS)
 sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, float* __restrict__ part, unsigned* __restrict__ counters,
-                   bf16* __restrict__ out, int Hq, int Hkv, int kv_len, int max_len, float scale_log2) {
+                   bf16* __restrict__ out, int Hq, int Hkv, int kv_len, int max_len, float scale_log2,
+                   const int32_t* __restrict__ kv_dev, int kv_add) {
   extern __shared__ __align__(1024) uint8_t sdpa_smem_raw[];
   uint8_t* sdpa_smem = sdpa_smem_raw + ((1024 - (smem_u32(sdpa_smem_raw) & 1023)) & 1023);
   uint8_t* ring = sdpa_smem;  // [stage][K|V][2 boxes][32 positions][128 B], 128-byte swizzle
@@ -143,12 +144,9 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
   float* mrg = reinterpret_cast<float*>(sdpa_smem);  // [warp][head][D + 2], reuses the ring after the math
   __shared__ int s_last;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int n_splits = gridDim.x;
   const int G = Hq / Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates: head row g, column pair c
-  const int t0 = split * SDPA_CHUNK;
-  const int t1 = min(kv_len, t0 + SDPA_CHUNK);
   const int row0 = ((int)b * Hkv + kvh) * max_len;  // this head's first cache row in the [rows, D] maps
 
   if (threadIdx.x == 0) {
@@ -158,6 +156,16 @@ sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorM
   __syncthreads();
   // the cache and q may come from the previous kernel (launch overlap): wait for it
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // a cache length held in device memory (one graph for every decode step): the grid covers
+  // the longest cache, and splits past this call's length leave before touching anything
+  if (kv_dev) {
+    kv_len = kv_dev[0] + kv_add;
+    if (kv_len < 1 || kv_len > max_len) return;
+  }
+  const int n_splits = (kv_len + SDPA_CHUNK - 1) / SDPA_CHUNK;
+  if (split >= n_splits) return;
+  const int t0 = split * SDPA_CHUNK;
+  const int t1 = min(kv_len, t0 + SDPA_CHUNK);
 
   const int nsub = t1 > t0 ? (t1 - t0 + SDPA_SUB - 1) / SDPA_SUB : 0;  // <= SDPA_STAGES
   auto kst = [&](int s) { return ring + ((size_t)s * 2 + 0) * SDPA_SUB * SDPA_D * 2; };
@@ -442,7 +450,8 @@ static size_t sdpa_ws_bytes(int64_t batch, int n_heads, int64_t kv_len) {
 
 static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
                        int64_t batch,
-                       int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st) {
+                       int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st,
+                       const int32_t* kv_dev = nullptr, int kv_add = 0) {
   {
     const int rc = ensure_max_dynamic_smem((const void*)sdpa_decode_kernel, (int)SDPA_SMEM);
     if (rc) return rc;
@@ -470,7 +479,7 @@ static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* 
   cfg.attrs = at;
   cfg.numAttrs = launch_overlap() ? 1 : 0;
   return check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel, q, tmk, tmv, part, counters, out, n_heads, n_kv_heads,
-                                       (int)kv_len, (int)max_len, scale * 1.4426950408889634f),
+                                       (int)kv_len, (int)max_len, scale * 1.4426950408889634f, kv_dev, kv_add),
                     "sdpa_decode_kernel launch");
 }
 
@@ -498,6 +507,31 @@ extern "C" int vmlx_cuda_sdpa_decode(void* out, const void* q, const void* k_cac
   return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, static_cast<unsigned*>(workspace),
                      reinterpret_cast<float*>(static_cast<char*>(workspace) + sdpa_cnt_bytes(batch, n_heads)),
                      (bf16*)out, batch, n_heads, n_kv_heads, kv_len, max_len, scale, as_stream(stream));
+}
+
+// Decode attention with the cache length read from device memory: kv_len = *pos_dev + 1 (the
+// token at position *pos_dev was just appended).  The grid and the workspace cover max_len,
+// so one captured graph serves every step of a token loop.
+extern "C" int vmlx_cuda_sdpa_decode_at(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                        int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                        const int32_t* pos_dev, int64_t max_len, float scale, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (!out || !q || !k_cache || !v_cache || !workspace || !pos_dev)
+    return set_error(VMLX_E_INVALID, "sdpa_decode_at: null pointer");
+  if (head_dim != SDPA_D) return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode_at: head_dim=%d (only 128)", head_dim);
+  if (n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
+    return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode_at: %d q heads per kv head (1..8 supported)",
+                     n_kv_heads > 0 ? n_heads / n_kv_heads : 0);
+  if (max_len <= 0) return set_error(VMLX_E_INVALID, "sdpa_decode_at: max_len=%lld", (long long)max_len);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(q, 16))
+    return set_error(VMLX_E_INVALID, "sdpa_decode_at: pointers must be 16-byte aligned");
+  const size_t need = vmlx_cuda_sdpa_decode_workspace(batch, n_heads, max_len, head_dim);
+  if (workspace_bytes < need)
+    return set_error(VMLX_E_INVALID, "sdpa_decode_at: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if (batch == 0) return VMLX_OK;
+  return sdpa_launch((const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, static_cast<unsigned*>(workspace),
+                     reinterpret_cast<float*>(static_cast<char*>(workspace) + sdpa_cnt_bytes(batch, n_heads)),
+                     (bf16*)out, batch, n_heads, n_kv_heads, max_len, max_len, scale, as_stream(stream), pos_dev, 1);
 }
 
 extern "C" int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, int64_t ffn, void* stream) {
