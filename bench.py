@@ -532,7 +532,7 @@ def bench_qwen3(args, torch, vm, dev):
     B, T = args.batch, args.ctx if args.ctx != 4096 else 2048
     vm.lib().vmlx_set_launch_overlap(1)
     n_e2e = max(8, args.steps // 2)
-    max_len = T + max(3, args.warmup) + args.steps + n_e2e + 8  # every replayed step appends one position
+    max_len = T + max(3, args.warmup) + args.steps + n_e2e + 16  # every replayed step appends one position
     dec = vm.qwen3.Qwen3Decoder(cfg, B, max_len=max_len, dev=dev, seed=0)
     prompt = torch.randint(0, cfg.vocab, (B, T), device=dev, generator=torch.Generator(device=dev).manual_seed(1))
     t0 = time.perf_counter()
@@ -581,6 +581,13 @@ def bench_qwen3(args, torch, vm, dev):
         e1.record(stream)
     torch.cuda.synchronize()
     t_e2e = e0.elapsed_time(e1) / 1e3 / n_e2e
+    if args.profile:  # one eager decode step inside an NVTX range (ncu --nvtx-include vmlx_profile/)
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("vmlx_profile")
+            dec.step()
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
     return {
         "metric": "decode tokens/s (Qwen3-32B-shaped greedy generation, 4-bit g64)",
         "value": round(B / t_step, 2), "unit": "tokens/s", "higher_is_better": True,

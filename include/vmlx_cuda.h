@@ -424,6 +424,21 @@ VMLX_API int vmlx_tp_quantized_matmul_swiglu_all_sum(void* tp, void* y, const vo
                                                      void* stream);
 
 /*
+ * The MoE block output under expert-intermediate tensor parallelism, in one kernel per rank:
+ *   out[t, :] = bf16([residual +] bf16(sum_r bf16(sum_j y_r[inverse_order[t*k + j], :] * scores[t, j])))
+ * i.e. vmlx_cuda_moe_combine on this rank's partial expert outputs y_r ([rows*k, dims], each rank
+ * holding its slice of every expert's intermediate dimension), all-reduced over the group with the
+ * low-latency word protocol of vmlx_tp_all_sum (counts as one all_sum call in the group's
+ * sequence; rows*dims*8 <= max_bytes).  Replaces scatterUnsort + the weighted sum
+ * (Libraries/MLXLMCommon/SwitchLayers.swift:77-83, Libraries/MLXLLM/Models/Qwen3MoE.swift:150-151)
+ * followed by Collectives.allSum (Libraries/MLXDistributedTP/Collectives.swift:27-32).  Size 1:
+ * the combine (+ residual).  residual may be NULL or alias out.
+ */
+VMLX_API int vmlx_tp_moe_combine_all_sum(void* tp, void* out, const void* y, const uint32_t* inverse_order,
+                                         const void* scores, int scores_dtype, int64_t rows, int k, int64_t dims,
+                                         const void* residual, void* stream);
+
+/*
  * Reads (synchronously) and clears the group's device status word:
  * *code = 0, or VMLX_E_PEER_TIMEOUT if some wait on a peer ran out since the
  * last read.

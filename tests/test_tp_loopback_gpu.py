@@ -169,3 +169,35 @@ def test_loopback_rejects_bad_world(vm, cuda):
     h = ctypes.c_void_p()
     assert vm.lib().vmlx_tp_create_loopback(1, 1 << 16, ctypes.byref(h)) != 0
     assert vm.lib().vmlx_tp_create_loopback(9, 1 << 16, ctypes.byref(h)) != 0
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("score_dtype", [torch.float32, torch.bfloat16])
+def test_loopback_moe_combine_all_sum(vm, cuda, world, score_dtype):
+    """The MoE block output under expert-intermediate TP: each rank's weighted combine of its
+    partial expert outputs, all-reduced in the same kernel.  Per rank it must equal the
+    separate combine kernel's output (bitwise), and the result the rank-order sum of those,
+    plus the residual."""
+    lib = vm.lib()
+    T, k, D = 33, 8, 2048
+    g = torch.Generator(device=cuda).manual_seed(world)
+    y = torch.randn(world, T * k, D, device=cuda, generator=g).bfloat16()
+    inv = torch.stack([torch.randperm(T * k, device=cuda, generator=g) for _ in range(world)]).to(torch.int32)
+    inv[1:] = inv[0]  # routing is replicated: every rank holds the same order and scores
+    sc = torch.rand(T, k, device=cuda, generator=g).to(score_dtype)
+    scores = sc.expand(world, T, k).contiguous()
+    res = torch.randn(T, D, device=cuda, generator=g).bfloat16().expand(world, T, D).contiguous()
+    h = _loopback(vm, world, max_bytes=T * D * 8)
+    out = torch.full((world, T, D), float("nan"), device=cuda, dtype=torch.bfloat16)
+    sd = vm._lib.VMLX_F32 if score_dtype == torch.float32 else vm._lib.VMLX_BF16
+    st = torch.cuda.current_stream().cuda_stream
+    rc = lib.vmlx_tp_moe_combine_all_sum(h, out.data_ptr(), y.data_ptr(), inv.data_ptr(), scores.data_ptr(), sd, T,
+                                         k, D, res.data_ptr(), st)
+    assert rc == 0, lib.vmlx_last_error()
+    torch.cuda.synchronize()
+    assert _status(vm, h) == 0
+    parts = [vm.ops.moe_combine(y[r], sc, inv[r]) for r in range(world)]
+    ref = vm.fast.add(_rank_order_sum(parts), res[0])
+    for r in range(world):
+        assert torch.equal(out[r], ref), r
+    lib.vmlx_tp_destroy(h)

@@ -73,6 +73,7 @@ SIGNATURES = {
     "vmlx_cuda_advance": (_int, [_vp, _c.c_int32, _vp]),
     "vmlx_tp_create": (_int, [_int, _int, _sz, _c.POINTER(_vp)]),
     "vmlx_tp_create_loopback": (_int, [_int, _sz, _c.POINTER(_vp)]),
+    "vmlx_tp_moe_combine_all_sum": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _i64, _int, _i64, _vp, _vp]),
     "vmlx_tp_rank": (_int, [_vp]),
     "vmlx_tp_size": (_int, [_vp]),
     "vmlx_tp_ipc_handle": (_int, [_vp, _vp]),

@@ -19,14 +19,14 @@ namespace vmlx {
 template <int BITS>
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ wq,
                              const bf16* __restrict__ scales, const bf16* __restrict__ biases,
-                             bf16* __restrict__ out, int vocab, int dims, int gs, int* status) {
-  const int r = blockIdx.x;
+                             bf16* __restrict__ out, int64_t n, int vocab, int dims, int gs, int* status) {
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
   const int id = ids[r];
-  bf16* orow = out + (int64_t)r * dims;
+  bf16* orow = out + r * dims;
   if (id < 0 || id >= vocab) {  // out of range: zeros and a status, never an out-of-bounds read
     for (int k = threadIdx.x; k < dims; k += blockDim.x) orow[k] = __float2bfloat16_rn(0.f);
     if (threadIdx.x == 0 && status) atomicExch(status, VMLX_E_INVALID);
-    return;
+    continue;
   }
   constexpr int PER = 32 / BITS;
   const int words = dims / PER;
@@ -44,6 +44,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __
       const float prod = __bfloat162float(__float2bfloat16_rn(__fmul_rn(s, q)));
       orow[k0 + j] = __float2bfloat16_rn(__fadd_rn(prod, b));
     }
+  }
   }
 }
 
@@ -165,18 +166,19 @@ extern "C" int vmlx_cuda_quantized_embedding(void* out, const int32_t* ids, cons
   if (bits != 2 && bits != 4 && bits != 8) return set_error(VMLX_E_UNSUPPORTED, "bits=%d not supported", bits);
   if (group_size != 32 && group_size != 64 && group_size != 128)
     return set_error(VMLX_E_UNSUPPORTED, "group_size=%d not supported", group_size);
-  if (n < 0 || n > 65535 || vocab <= 0 || vocab >= (1LL << 31) || dims <= 0 || dims % group_size)
+  if (n < 0 || n >= (1LL << 31) || vocab <= 0 || vocab >= (1LL << 31) || dims <= 0 || dims % group_size)
     return set_error(VMLX_E_INVALID, "quantized_embedding: n=%lld vocab=%lld dims=%lld", (long long)n,
                      (long long)vocab, (long long)dims);
   const cudaStream_t st = as_stream(stream);
+  const unsigned grid = (unsigned)(n < 65535 ? n : 65535);
   if (bits == 2)
-    embed_kernel<2><<<(unsigned)n, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out,
+    embed_kernel<2><<<grid, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out, n,
                                                  (int)vocab, (int)dims, group_size, status);
   else if (bits == 4)
-    embed_kernel<4><<<(unsigned)n, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out,
+    embed_kernel<4><<<grid, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out, n,
                                                  (int)vocab, (int)dims, group_size, status);
   else
-    embed_kernel<8><<<(unsigned)n, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out,
+    embed_kernel<8><<<grid, 256, 0, st>>>(ids, w, (const bf16*)scales, (const bf16*)biases, (bf16*)out, n,
                                                  (int)vocab, (int)dims, group_size, status);
   return check_launch("embed_kernel");
 }

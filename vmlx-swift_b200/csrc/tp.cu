@@ -205,6 +205,95 @@ tp_all_sum_ll_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const
   if (threadIdx.x == 0) tp_advance_epoch(epoch_p, e);
 }
 
+// MoE block output under expert-intermediate TP: scatterUnsort + score-weighted sum of this
+// rank's partial expert outputs (vmlx_cuda_moe_combine's arithmetic, rounded to bf16 per rank),
+// all-reduced over the group in the same kernel (the low-latency word protocol of
+// tp_all_sum_ll_kernel, same slots and epochs: it is one more all_sum call in the group's
+// sequence), optionally plus a residual.  One thread = 8 consecutive outputs of one token row.
+// The epoch is advanced by the grid's last CTA (of gridDim.x * gridDim.y per rank).
+template <typename TS>
+__global__ void __launch_bounds__(128)
+tp_moe_combine_kernel(TpPeers peers, int rank, int world, size_t max_bytes, const bf16* __restrict__ y,
+                      const uint32_t* __restrict__ inv, const TS* __restrict__ scores, int64_t T, int k, int64_t D,
+                      const bf16* __restrict__ residual, bf16* __restrict__ out, int* status, uint64_t timeout_ns,
+                      int loop) {
+  if (loop) {  // loopback group: rank = blockIdx.z, every operand stacked along a leading rank axis
+    rank = blockIdx.z;
+    y += (int64_t)rank * T * k * D;
+    if (inv) inv += (int64_t)rank * T * k;
+    scores += (int64_t)rank * T * k;
+    out += (int64_t)rank * T * D;
+    if (residual) residual += (int64_t)rank * T * D;
+  }
+  char* mine = peers.buf[rank];
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(mine + tp_epoch_off(max_bytes, world));
+  __shared__ uint32_t s_epoch;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) s_epoch = epoch_p[0] + 1;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int parity = e & 1;
+  const int64_t t = blockIdx.y;
+  const int64_t d0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const bool act = d0 < D;
+  // 1. this rank's combined partial, rounded to bf16 as the separate combine kernel does
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (act) {
+    for (int j = 0; j < k; j++) {
+      const int64_t pair = t * k + j;
+      const int64_t src = inv ? (int64_t)inv[pair] : pair;
+      float sc;
+      if constexpr (sizeof(TS) == 4) sc = scores[pair];
+      else sc = __bfloat162float(scores[pair]);
+      const uint4 v = *reinterpret_cast<const uint4*>(y + src * D + d0);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __bfloat1622float2(u32_as_bf162(u[q]));
+        float p0 = f.x * sc, p1 = f.y * sc;
+        if constexpr (sizeof(TS) == 2) {  // bf16 scores: each product rounds to bf16 (MLX's bf16 multiply)
+          p0 = __bfloat162float(__float2bfloat16_rn(p0));
+          p1 = __bfloat162float(__float2bfloat16_rn(p1));
+        }
+        acc[2 * q] += p0;
+        acc[2 * q + 1] += p1;
+      }
+    }
+    // 2. push the 8 bf16 partials to every rank as {value, epoch} words
+    for (int r = 0; r < world; r++) {
+      uint64_t* dst = reinterpret_cast<uint64_t*>(peers.buf[r] + tp_ll_slot_off(parity, rank, max_bytes, world)) +
+                      t * D + d0;
+#pragma unroll
+      for (int q = 0; q < 8; q++) st_ll(dst + q, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc[q])), e);
+    }
+  }
+  // 3. sum every rank's words of these outputs in rank order (bounded waits)
+  bool ok = true;
+  if (act) {
+    const uint64_t deadline = globaltimer() + timeout_ns;
+    const uint64_t* slots = reinterpret_cast<const uint64_t*>(mine + tp_ll_slot_off(parity, 0, max_bytes, world));
+    const size_t rstride = max_bytes / sizeof(uint64_t);
+    for (int q = 0; q < 8 && ok; q++) {
+      float sum;
+      ok = wait_ll_sum<TP_MAX_WORLD>(slots + t * D + d0 + q, rstride, world, e, deadline, sum);
+      if (!ok) break;
+      const int64_t idx = t * D + d0 + q;
+      const bf16 sb = __float2bfloat16_rn(sum);
+      out[idx] = residual ? __float2bfloat16_rn(__bfloat162float(residual[idx]) + __bfloat162float(sb)) : sb;
+    }
+    if (!ok) atomicExch(status, VMLX_E_PEER_TIMEOUT);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(epoch_p + 1, 1u) == gridDim.x * gridDim.y - 1) {
+      epoch_p[1] = 0;
+      epoch_p[0] = e;
+      __threadfence();
+    }
+  }
+}
+
 static int tp_check(TpHandle* h) {
   if (!h) return set_error(VMLX_E_INVALID, "tp: null handle");
   return VMLX_OK;
@@ -446,6 +535,56 @@ static int tp_qmm_all_sum(void* tp, void* y, const void* x, const uint32_t* w, c
   a.tp_loop = h->loop ? 1 : 0;
   if (swiglu && K % 8) return set_error(VMLX_E_INVALID, "tp: SwiGLU input needs K a multiple of 8");
   return launch_qmv(a, QMV_DENSE, bits, group_size, 1, (int)M, as_stream(stream));
+}
+
+extern "C" int vmlx_tp_moe_combine_all_sum(void* tp, void* out, const void* y, const uint32_t* inverse_order,
+                                           const void* scores, int scores_dtype, int64_t rows, int k, int64_t dims,
+                                           const void* residual, void* stream) {
+  TpHandle* h = static_cast<TpHandle*>(tp);
+  int rc = tp_check(h);
+  if (rc) return rc;
+  if (rows < 0 || k < 1 || dims < 1) return set_error(VMLX_E_INVALID, "tp_moe_combine_all_sum: bad shape");
+  if (rows == 0) return VMLX_OK;
+  if (!out || !y || !scores) return set_error(VMLX_E_INVALID, "tp_moe_combine_all_sum: null pointer");
+  if (dims % 8 || !aligned(y, 16)) return set_error(VMLX_E_INVALID, "tp_moe_combine_all_sum: dims must be a multiple of 8");
+  if (rows > 65535) return set_error(VMLX_E_UNSUPPORTED, "tp_moe_combine_all_sum: rows=%lld > 65535", (long long)rows);
+  if (scores_dtype != VMLX_F32 && scores_dtype != VMLX_BF16)
+    return set_error(VMLX_E_UNSUPPORTED, "tp_moe_combine_all_sum: scores dtype %d", scores_dtype);
+  if (h->world == 1) {  // a size-1 group: the combine, then the residual add
+    rc = vmlx_cuda_moe_combine(y, inverse_order, scores, scores_dtype, rows, k, dims, out, stream);
+    if (rc || !residual) return rc;
+    return vmlx_cuda_add(out, residual, out, rows * dims, stream);
+  }
+  if (!h->connected) return set_error(VMLX_E_STATE, "tp_moe_combine_all_sum: peers not connected");
+  if ((size_t)rows * dims * 8 > h->max_bytes)
+    return set_error(VMLX_E_INVALID, "tp_moe_combine_all_sum: %lld x %lld output exceeds the %zu-byte slots",
+                     (long long)rows, (long long)dims, h->max_bytes);
+  TpPeers peers;
+  for (int r = 0; r < TP_MAX_WORLD; r++) peers.buf[r] = r < h->world ? h->peer_base[r] : nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((dims / 8 + 127) / 128), (unsigned)rows, h->loop ? (unsigned)h->world : 1u);
+  cfg.blockDim = dim3(128);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr;
+  // every CTA waits for the other ranks' words: all CTAs must be resident together (a
+  // cooperative launch for the loopback group, whose ranks share this GPU)
+  if (h->loop) {
+    attr.id = cudaLaunchAttributeCooperative;
+    attr.val.cooperative = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+  }
+  const int rank = h->loop ? 0 : h->rank, loop = h->loop ? 1 : 0;
+  cudaError_t e;
+  if (scores_dtype == VMLX_F32)
+    e = cudaLaunchKernelEx(&cfg, tp_moe_combine_kernel<float>, peers, rank, h->world, h->max_bytes, (const bf16*)y,
+                           inverse_order, (const float*)scores, rows, k, dims, (const bf16*)residual, (bf16*)out,
+                           h->status, h->timeout_ns, loop);
+  else
+    e = cudaLaunchKernelEx(&cfg, tp_moe_combine_kernel<bf16>, peers, rank, h->world, h->max_bytes, (const bf16*)y,
+                           inverse_order, (const bf16*)scores, rows, k, dims, (const bf16*)residual, (bf16*)out,
+                           h->status, h->timeout_ns, loop);
+  return check_cuda(e, "tp_moe_combine_kernel launch");
 }
 
 extern "C" int vmlx_tp_status(void* tp, int* code) {

@@ -25,7 +25,7 @@ from typing import List, Optional
 
 import torch
 
-from . import _lib, fast
+from . import _lib, fast, ops
 from ._lib import VMLXError, check
 from .llama import QuantLinear, shard_k, shard_rows
 from .ops import _stream
@@ -89,6 +89,24 @@ class Group:
             return x if out is None else out.copy_(x)
         out = x if out is None else out
         check(_lib.lib().vmlx_tp_all_sum(self._h, out.data_ptr(), x.data_ptr(), x.numel(), _stream(x)))
+        return out
+
+    def moe_combine_all_sum(self, y: torch.Tensor, scores: torch.Tensor, inverse_order: Optional[torch.Tensor],
+                            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
+                            ) -> torch.Tensor:
+        """out [T, D] = [residual +] all_sum over the group of the score-weighted combine of this
+        rank's partial expert outputs y [T*k, D] (one kernel per rank)."""
+        T, k = scores.shape
+        D = y.shape[-1]
+        out = torch.empty(T, D, dtype=torch.bfloat16, device=y.device) if out is None else out
+        sd = _lib.VMLX_F32 if scores.dtype == torch.float32 else _lib.VMLX_BF16
+        if self._h is None:  # size-1 group: the plain combine
+            r = ops.moe_combine(y, scores, inverse_order)
+            return r if residual is None else fast.add(r, residual, out=out)
+        check(_lib.lib().vmlx_tp_moe_combine_all_sum(
+            self._h, out.data_ptr(), y.contiguous().data_ptr(),
+            inverse_order.data_ptr() if inverse_order is not None else None, scores.contiguous().data_ptr(), sd,
+            T, k, D, residual.data_ptr() if residual is not None else None, _stream(y)))
         return out
 
     def quantized_matmul_all_sum(self, x: torch.Tensor, ql: "QuantLinear", residual: Optional[torch.Tensor] = None,
@@ -211,7 +229,10 @@ class ShardedSwitchGLU:
         self.local = SwitchGLU(rows(gp), rows(up), down)
         self.group, self.groups = group, (g0, g1)
 
-    def combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
-        """sum_j SwitchGLU(x, indices)[:, j] * scores[:, j], reduced over the group."""
-        y = self.local.combined(x, indices, scores)
-        return self.group.all_sum(y)
+    def combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor,
+                 residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """[residual +] sum_j SwitchGLU(x, indices)[:, j] * scores[:, j], reduced over the group:
+        the weighted combine and the all-reduce run as one kernel (vmlx_tp_moe_combine_all_sum)."""
+        y, inv = self.local._expert_outputs(x, indices)
+        T = indices.reshape(-1, indices.shape[-1]).shape[0]
+        return self.group.moe_combine_all_sum(y.reshape(-1, y.shape[-1]), scores.reshape(T, -1), inv, residual)

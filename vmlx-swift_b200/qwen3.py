@@ -132,8 +132,10 @@ class Qwen3Decoder:
         for i, L in enumerate(self.layers):
             fast.rms_norm(x, L.norm1, cfg.eps, out=h)
             qkv = L.qkv(h)
-            fast.rope_qk_norm(qkv, self.k_cache[i], self.v_cache[i], Hq, Hkv, 0, L.q_norm, L.k_norm, cfg.eps,
-                              cfg.rope_theta, tokens_per_seq=T, q_out=q, status=self.status)
+            for s in range(B):  # one call per sequence: its T rows at positions 0..T-1
+                rs = slice(s * T, (s + 1) * T)
+                fast.rope_qk_norm(qkv[rs], self.k_cache[i][s:s + 1], self.v_cache[i][s:s + 1], Hq, Hkv, 0, L.q_norm,
+                                  L.k_norm, cfg.eps, cfg.rope_theta, tokens_per_seq=T, q_out=q[rs], status=self.status)
             qh = q.view(B, T, Hq, D).transpose(1, 2)
             kh = self.k_cache[i][:, :, :T]
             vh = self.v_cache[i][:, :, :T]
