@@ -227,7 +227,7 @@ def bench_gemv(args, torch, vm, dev):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                      "frac_of_8TBps": round(achieved / 8000, 4),
-                     "traffic": load_traffic("qmv_kernel_4096x4096_b4_M1"),
+                     "traffic": load_traffic("qgemv_kernel_4096x4096_b4_M1"),
                      "algorithmic_bytes_per_launch": nbytes},
         "e2e": {"value": round(nbytes / t_e2e / 1e9, 2), "unit": "GB/s", "us_per_call": round(t_e2e * 1e6, 2),
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
