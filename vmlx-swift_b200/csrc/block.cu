@@ -107,7 +107,7 @@ __global__ void rope_qkv_kernel(const bf16* __restrict__ qkv, bf16* __restrict__
 }
 
 // ------------------------------------------------------------ decode SDPA --
-// One CTA per (cache split of up to 256 positions, kv head, sequence), 8 warps:
+// One CTA per (cache split of 128 or 256 positions, kv head, sequence), 4 or 8 warps:
 // warp w takes the split's 32-position stage w.  K and V arrive as 2-D TMA boxes
 // [32 positions x 64 dims] with the 128-byte swizzle (the whole split is in
 // flight at once).  The math runs on the tensor cores (mma.sync m16n8k16, bf16
@@ -120,11 +120,18 @@ __global__ void rope_qkv_kernel(const bf16* __restrict__ qkv, bf16* __restrict__
 // -- combines the splits (flash-decoding) and writes the output.
 constexpr int SDPA_D = 128;
 constexpr int SDPA_SUB = 32;     // positions per stage (one warp each)
-constexpr int SDPA_STAGES = 8;   // stages per split: 8 x (K + V) x 32 positions = 128 KB
-constexpr int SDPA_CHUNK = SDPA_SUB * SDPA_STAGES;  // positions per split
-constexpr int SDPA_THREADS = 32 * SDPA_STAGES;
-constexpr size_t SDPA_RING = (size_t)SDPA_STAGES * 2 * SDPA_SUB * SDPA_D * sizeof(bf16);
-constexpr size_t SDPA_SMEM = SDPA_RING + 64 + 1024;  // + alignment slack
+// Stages per split (a template parameter of the kernel): 8 (256 positions, 128 KB of K/V in
+// flight, one CTA per SM) while the grid is small, 4 (128 positions, 64 KB, 2-3 CTAs per SM)
+// once it covers the SMs twice over, where more resident warps per SM hide the latencies.
+constexpr int SDPA_MAX_STAGES = 8;
+constexpr int SDPA_MIN_CHUNK = SDPA_SUB * 4;  // the smallest split: workspaces are sized for it
+template <int ST> struct SdpaCfg {
+  static constexpr int STAGES = ST;
+  static constexpr int CHUNK = SDPA_SUB * ST;  // positions per split
+  static constexpr int THREADS = 32 * ST;
+  static constexpr size_t RING = (size_t)ST * 2 * SDPA_SUB * SDPA_D * sizeof(bf16);
+  static constexpr size_t SMEM = RING + 64 + 1024;  // + alignment slack
+};
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -132,11 +139,14 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                : "r"(addr));
 }
 
-__global__ void __launch_bounds__(SDPA_THREADS)
+template <int ST>
+__global__ void __launch_bounds__(SdpaCfg<ST>::THREADS)
 sdpa_decode_kernel(const bf16* __restrict__ q, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, float* __restrict__ part, unsigned* __restrict__ counters,
                    bf16* __restrict__ out, int Hq, int Hkv, int kv_len, int max_len, float scale_log2,
                    const int32_t* __restrict__ kv_dev, int kv_add) {
+  constexpr int SDPA_STAGES = SdpaCfg<ST>::STAGES, SDPA_CHUNK = SdpaCfg<ST>::CHUNK, SDPA_THREADS = SdpaCfg<ST>::THREADS;
+  constexpr size_t SDPA_RING = SdpaCfg<ST>::RING;
   extern __shared__ __align__(1024) uint8_t sdpa_smem_raw[];
   uint8_t* sdpa_smem = sdpa_smem_raw + ((1024 - (smem_u32(sdpa_smem_raw) & 1023)) & 1023);
   uint8_t* ring = sdpa_smem;  // [stage][K|V][2 boxes][32 positions][128 B], 128-byte swizzle
@@ -431,8 +441,8 @@ extern "C" int vmlx_cuda_rope_qkv(void* q_out, void* k_cache, void* v_cache, con
   return check_launch("vmlx_cuda_rope_qkv");
 }
 
-static int sdpa_splits(int64_t kv_len) {
-  const int64_t s = (kv_len + SDPA_CHUNK - 1) / SDPA_CHUNK;  // SDPA_CHUNK cache positions per CTA
+static int sdpa_splits(int64_t kv_len, int chunk = SDPA_MIN_CHUNK) {
+  const int64_t s = (kv_len + chunk - 1) / chunk;  // chunk cache positions per CTA
   return (int)(s < 1 ? 1 : s);
 }
 
@@ -448,17 +458,19 @@ static size_t sdpa_ws_bytes(int64_t batch, int n_heads, int64_t kv_len) {
   return sdpa_cnt_bytes(batch, n_heads) + sdpa_part_bytes(batch, n_heads, kv_len);
 }
 
-static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
-                       int64_t batch,
-                       int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale, cudaStream_t st,
-                       const int32_t* kv_dev = nullptr, int kv_add = 0) {
+template <int ST>
+static int sdpa_launch_st(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
+                          int64_t batch, int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale,
+                          cudaStream_t st, const int32_t* kv_dev, int kv_add) {
+  using C = SdpaCfg<ST>;
+  auto kern = sdpa_decode_kernel<ST>;
   {
-    const int rc = ensure_max_dynamic_smem((const void*)sdpa_decode_kernel, (int)SDPA_SMEM);
+    const int rc = ensure_max_dynamic_smem((const void*)kern, (int)C::SMEM);
     if (rc) return rc;
   }
-  const int splits = sdpa_splits(kv_len);
+  const int splits = sdpa_splits(kv_len, C::CHUNK);
   // the combining CTA keeps m and l per (head, split) in the ring
-  if (splits > 65535 || (size_t)(2 * splits + 1) * (n_heads / n_kv_heads) * sizeof(float) > SDPA_RING)
+  if (splits > 65535 || (size_t)(2 * splits + 1) * (n_heads / n_kv_heads) * sizeof(float) > C::RING)
     return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: kv_len=%lld too long", (long long)kv_len);
   const int64_t rows = batch * n_kv_heads * max_len;
   if (rows >= (1LL << 31)) return set_error(VMLX_E_UNSUPPORTED, "sdpa_decode: cache of %lld rows", (long long)rows);
@@ -470,18 +482,32 @@ static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* 
     return VMLX_E_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)splits, (unsigned)n_kv_heads, (unsigned)batch);
-  cfg.blockDim = dim3(SDPA_THREADS);
-  cfg.dynamicSmemBytes = SDPA_SMEM;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = launch_overlap() ? 1 : 0;
-  return check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel, q, tmk, tmv, part, counters, out, n_heads, n_kv_heads,
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, q, tmk, tmv, part, counters, out, n_heads, n_kv_heads,
                                        (int)kv_len, (int)max_len, scale * 1.4426950408889634f, kv_dev, kv_add),
                     "sdpa_decode_kernel launch");
 }
+
+// Split size from the grid it gives (never from the data): 256-position splits while they give
+// fewer than two CTAs per SM, 128-position splits (smaller CTAs, 2-3 per SM) beyond.
+static int sdpa_launch(const bf16* q, const bf16* kc, const bf16* vc, unsigned* counters, float* part, bf16* out,
+                       int64_t batch, int n_heads, int n_kv_heads, int64_t kv_len, int64_t max_len, float scale,
+                       cudaStream_t st, const int32_t* kv_dev = nullptr, int kv_add = 0) {
+  const int64_t ctas8 = (int64_t)sdpa_splits(kv_len, SdpaCfg<8>::CHUNK) * n_kv_heads * batch;
+  if (ctas8 < 2 * (int64_t)sm_count())
+    return sdpa_launch_st<8>(q, kc, vc, counters, part, out, batch, n_heads, n_kv_heads, kv_len, max_len, scale, st,
+                             kv_dev, kv_add);
+  return sdpa_launch_st<4>(q, kc, vc, counters, part, out, batch, n_heads, n_kv_heads, kv_len, max_len, scale, st,
+                           kv_dev, kv_add);
+}
+
 
 extern "C" size_t vmlx_cuda_sdpa_decode_workspace(int64_t batch, int n_heads, int64_t kv_len, int head_dim) {
   (void)head_dim;
