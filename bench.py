@@ -463,7 +463,8 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
         w_tp = sum(L.o.nbytes + L.down.nbytes for L in dec.layers) / len(tp_calls)
         link = (world - 1) * B * cfg.hidden * 2  # bf16 partial rows sent to the other ranks per call
         t_target = max(w_tp / (hbm * 1e9), link / 770e9)
-        tp_fused = {"kernel": "qmv_kernel with the row-parallel all-reduce (vmlx_tp_quantized_matmul_all_sum)",
+        tp_fused = {"kernel": "qgemv_kernel / qmv_kernel with the row-parallel all-reduce "
+                              "(vmlx_tp_quantized_matmul_all_sum)",
                     "us_per_call": round(t_tp * 1e6, 2), "weight_bytes_per_call": int(w_tp),
                     "nvlink_bytes_out_per_call": link,
                     "unfused_us_per_call": round(t_unf * 1e6, 2),

@@ -404,7 +404,7 @@ VMLX_API int vmlx_tp_all_sum(void* tp, void* out, const void* in, int64_t n, voi
  * One kernel per rank: the GEMV pushes its bf16 partial rows into every rank's
  * slot over NVLink P2P as 8-byte {value, epoch} words; each CTA then polls
  * (bounded) the words of the rows it computed and sums them in rank order, so y has the same bits on
- * every rank.  The partial rows come from the 1-32-row GEMV kernel's TP instance; the separate
+ * every rank.  The partial rows come from the TP instance of the GEMV kernel for the shape; the separate
  * quantized_matmul -> vmlx_tp_all_sum -> add chain may pick another GEMV kernel for the partials and
  * then agrees within the GEMV tolerance, not bitwise.  residual may be NULL or alias y.
  * Every rank must make the same sequence of calls.  Size 1: the local fused GEMV.

@@ -101,7 +101,8 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 // `dst` ([scale | bias][16*S rows][sbrow bytes]).  Asynchronous (cp.async; one commit
 // group per call, empty when !valid) when rows are 16-byte aligned, else plain loads.
 __device__ __forceinline__ void qg_load_scales(const QmvArgs& p, const QgGeom& g, uint8_t* dst, int64_t row0,
-                                               int64_t KG, int64_t cg0, int ncg, bool valid, int tid) {
+                                               int64_t KG, int64_t cg0, int ncg, bool valid, int tid,
+                                               int64_t roff) {
   const int rows = 16 * g.S;
   if (valid) {
     if (g.sc_async) {
@@ -109,7 +110,7 @@ __device__ __forceinline__ void qg_load_scales(const QmvArgs& p, const QgGeom& g
       for (int i = tid; i < 2 * rows * nchunk; i += QG_THREADS) {
         const int kind = i / (rows * nchunk), rem = i - kind * rows * nchunk;
         const int r = rem / nchunk, ch = rem - r * nchunk;
-        const int64_t row = row0 + r < p.N ? row0 + r : p.N - 1;
+        const int64_t row = roff + (row0 + r < p.N ? row0 + r : p.N - 1);
         const bf16* src = (kind ? p.biases : p.scales) + row * KG + cg0 + ch * 8;
         cp_async16(dst + ((size_t)kind * rows + r) * g.sbrow + ch * 16, src);
       }
@@ -117,13 +118,34 @@ __device__ __forceinline__ void qg_load_scales(const QmvArgs& p, const QgGeom& g
       for (int i = tid; i < 2 * rows * ncg; i += QG_THREADS) {
         const int kind = i / (rows * ncg), rem = i - kind * rows * ncg;
         const int r = rem / ncg, gl = rem - r * ncg;
-        const int64_t row = row0 + r < p.N ? row0 + r : p.N - 1;
+        const int64_t row = roff + (row0 + r < p.N ? row0 + r : p.N - 1);
         reinterpret_cast<bf16*>(dst + ((size_t)kind * rows + r) * g.sbrow)[gl] =
             (kind ? p.biases : p.scales)[row * KG + cg0 + gl];
       }
     }
   }
   cp_async_commit();
+}
+
+// One output element: y = bf16([residual +] bf16(v)); under row-parallel TP the bf16 partial
+// goes instead to slot [parity][rank] of every rank's buffer as a {value, epoch} word (P2P
+// stores; the reduction over the ranks runs after the tile loop).
+__device__ __forceinline__ void qg_store(const QmvArgs& p, int64_t idx, float v, bool tp, int trank, int64_t ybias,
+                                         uint32_t tp_e) {
+  if (tp) {
+    const uint32_t hv = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+    const size_t off = p.tp_slots_off + ((size_t)(tp_e & 1) * p.tp_world + trank) * p.tp_slot_bytes +
+                       (size_t)idx * sizeof(uint64_t);
+    for (int r = 0; r < p.tp_world; r++) st_ll(reinterpret_cast<uint64_t*>(p.tp_buf[r] + off), hv, tp_e);
+    return;
+  }
+  idx += ybias;
+  if (p.residual) {
+    const float sv = __bfloat162float(__float2bfloat16_rn(v));
+    p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
+  } else {
+    p.y[idx] = __float2bfloat16_rn(v);
+  }
 }
 
 template <int GS, int MT>
@@ -141,6 +163,14 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
 
   const int S = g.S, C = g.C;
   const int M = MT;
+  // Row-parallel TP (tp_world > 1): trank = this CTA's rank; lr = the same for a loopback group
+  // (all ranks in one grid, rank = blockIdx.y, operands stacked along a rank axis), else 0.
+  const bool tp = p.tp_world > 1;
+  const int lr = (tp && p.tp_loop) ? (int)blockIdx.y : 0;
+  const int trank = tp ? (p.tp_loop ? lr : p.tp_rank) : 0;
+  const int64_t wroff = (int64_t)lr * p.N;     // first weight / scale row of this rank's shard
+  const int64_t xrow0 = (int64_t)lr * M;       // first x row of this rank
+  const int64_t ybias = (int64_t)lr * M * p.N;  // offset of this rank's y / residual
   const int crank = C > 1 ? (int)(blockIdx.x % C) : 0;
   const int64_t cluster_id = blockIdx.x / C, nclusters = gridDim.x / C;
   const int64_t KG = p.K / GS;
@@ -180,7 +210,7 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
   const int x0 = (int)((cg0 + wg0) * GB);
   auto issue = [&](int st) {
     mbar_arrive_expect_tx(&bars[st], QG_STAGE_BYTES);
-    tma_load_2d(ring + st * QG_STAGE_BYTES, &tmw, x0 + iss_jj * (GC * GB), iss_row, &bars[st]);
+    tma_load_2d(ring + st * QG_STAGE_BYTES, &tmw, x0 + iss_jj * (GC * GB), iss_row + (int)wroff, &bars[st]);
     if (++iss_jj == nch) {
       iss_jj = 0;
       iss_row += row_step;
@@ -190,15 +220,18 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
     tma_prefetch_desc(&tmw);
     for (int j = 0; j < total_st && j < QG_STAGES; j++) issue(j);
   }
-  qg_load_scales(p, g, smem + L.o_sc, cluster_id * rows, KG, cg0, ncg, ntl > 0, tid);
-  qg_load_scales(p, g, smem + L.o_sc + scbuf, (cluster_id + nclusters) * rows, KG, cg0, ncg, ntl > 1, tid);
+  qg_load_scales(p, g, smem + L.o_sc, cluster_id * rows, KG, cg0, ncg, ntl > 0, tid, wroff);
+  qg_load_scales(p, g, smem + L.o_sc + scbuf, (cluster_id + nclusters) * rows, KG, cg0, ncg, ntl > 1, tid, wroff);
 
   // x may be written by the previous kernel
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // TP: this call's epoch (advanced by the previous call's last CTA) picks the slot parity
+  __shared__ uint32_t s_tp_e;
+  if (tp && tid == 0) s_tp_e = *reinterpret_cast<const uint32_t*>(p.tp_buf[trank] + p.tp_epoch_off) + 1;
   if (p.norm_w) {
     // fused RMSNorm: 1 / rms over each token's full row (the order of the other GEMV kernel)
     for (int t = warp; t < M; t += QG_WARPS) {
-      const bf16* xr = p.x + (int64_t)t * p.K;
+      const bf16* xr = p.x + (xrow0 + t) * p.K;
       float ss = 0.f;
 #pragma unroll 4
       for (int64_t k = lane * 8; k < p.K; k += 256) {
@@ -230,7 +263,7 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
         v[b] = u[b] = make_uint4(0, 0, 0, 0);
         if (i < total) {
           const int t = i / nkb, kb = i - t * nkb;
-          const bf16* xr = p.x + t * xrs + cg0 * GS + (int64_t)kb * 8;
+          const bf16* xr = p.x + (xrow0 + t) * xrs + cg0 * GS + (int64_t)kb * 8;
           v[b] = *reinterpret_cast<const uint4*>(xr);
           if (p.x_swiglu) u[b] = *reinterpret_cast<const uint4*>(xr + p.K);
         }
@@ -375,7 +408,7 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
     // ---- fixed-order reduction: warps of the CTA, then the CTAs of the cluster ----
     __syncthreads();
     // the buffer of this tile's scales is free: start copying the scales two tiles ahead
-    qg_load_scales(p, g, scb, (cluster_id + (ti + 2) * nclusters) * rows, KG, cg0, ncg, ti + 2 < ntl, tid);
+    qg_load_scales(p, g, scb, (cluster_id + (ti + 2) * nclusters) * rows, KG, cg0, ncg, ti + 2 < ntl, tid, wroff);
     const int KSPLIT = QG_WARPS / S;
     for (int i = tid; i < rows * M; i += QG_THREADS) {
       const int r = i / M, t = i - r * M;
@@ -384,15 +417,7 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
       for (int q = 0; q < KSPLIT; q++) v += red[((size_t)(q * S + ss_) * 16 + rr) * QG_TOKP + t];
       if (C == 1) {
         const int64_t n = row0 + r;
-        if (n < p.N) {
-          const int64_t idx = (int64_t)t * p.N + n;
-          if (p.residual) {
-            const float sv = __bfloat162float(__float2bfloat16_rn(v));
-            p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
-          } else {
-            p.y[idx] = __float2bfloat16_rn(v);
-          }
-        }
+        if (n < p.N) qg_store(p, (int64_t)t * p.N + n, v, tp, trank, ybias, tp ? s_tp_e : 0u);
       } else {
         ctile[r * QG_TOKP + t] = v;
       }
@@ -407,18 +432,48 @@ qgemv_kernel(QmvArgs p, QgGeom g, const __grid_constant__ CUtensorMap tmw) {
         float v = 0.f;
         for (int q = 0; q < C; q++) v += cluster.map_shared_rank(ctile, q)[r * QG_TOKP + t];
         const int64_t n = row0 + r;
-        if (n < p.N) {
-          const int64_t idx = (int64_t)t * p.N + n;
-          if (p.residual) {
-            const float sv = __bfloat162float(__float2bfloat16_rn(v));
-            p.y[idx] = __float2bfloat16_rn(__bfloat162float(p.residual[idx]) + sv);
-          } else {
-            p.y[idx] = __float2bfloat16_rn(v);
-          }
-        }
+        if (n < p.N) qg_store(p, (int64_t)t * p.N + n, v, tp, trank, ybias, tp ? s_tp_e : 0u);
       }
       cluster_arrive();  // peers have read this CTA's tile before it is overwritten or freed
       cluster_wait();
+    }
+  }
+  if (tp) {
+    // ---- row-parallel all-reduce: the rows this CTA wrote, from every rank, in rank order ----
+    // (each word is polled until it carries this call's epoch; every CTA of every rank is
+    // resident, the grid being one persistent wave)
+    const uint32_t e = s_tp_e;
+    const uint64_t deadline = globaltimer() + p.tp_timeout_ns;
+    const uint64_t* slots = reinterpret_cast<const uint64_t*>(p.tp_buf[trank] + p.tp_slots_off +
+                                                              (size_t)(e & 1) * p.tp_world * p.tp_slot_bytes);
+    const size_t rstride = p.tp_slot_bytes / sizeof(uint64_t);
+    const int rlo = C > 1 ? crank * rows / C : 0, rhi = C > 1 ? (crank + 1) * rows / C : rows;
+    bool tp_ok = true;
+    for (int64_t ti = 0; ti < ntl && tp_ok; ti++) {
+      const int64_t row0 = (cluster_id + ti * nclusters) * rows;
+      for (int i = tid; i < (rhi - rlo) * M && tp_ok; i += QG_THREADS) {
+        const int r = rlo + i / M, t = i % M;
+        const int64_t n = row0 + r;
+        if (n >= p.N) continue;
+        const int64_t idx = (int64_t)t * p.N + n;
+        float sum;
+        tp_ok = wait_ll_sum<QMV_TP_MAX_WORLD>(slots + idx, rstride, p.tp_world, e, deadline, sum);
+        if (!tp_ok) break;
+        const bf16 sb = __float2bfloat16_rn(sum);
+        const int64_t yi = idx + ybias;
+        p.y[yi] = p.residual ? __float2bfloat16_rn(__bfloat162float(p.residual[yi]) + __bfloat162float(sb)) : sb;
+      }
+    }
+    if (!tp_ok && p.tp_status) atomicExch(p.tp_status, VMLX_E_PEER_TIMEOUT);
+    __syncthreads();
+    if (tid == 0) {  // the grid's last CTA (of this rank) advances the epoch for the next call
+      uint32_t* ep = reinterpret_cast<uint32_t*>(p.tp_buf[trank] + p.tp_epoch_off);
+      __threadfence();
+      if (atomicAdd(ep + 1, 1u) == gridDim.x - 1) {
+        ep[1] = 0;
+        ep[0] = e;
+        __threadfence();
+      }
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -516,9 +571,33 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
     const int rc = ensure_max_dynamic_smem((const void*)kern, 220 * 1024);
     if (rc) return rc;
   }
-  const int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(L, MT) / g.C);
+  // A loopback TP group runs every rank's grid in one launch: the ranks share the SMs.
+  const int ranks = (a.tp_world > 1 && a.tp_loop) ? a.tp_world : 1;
+  int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(L, MT) / g.C / ranks);
+  if (a.tp_world > 1) {
+    // every CTA waits for the other ranks after its own rows: the whole grid must be resident
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3((unsigned)g.C, 1, 1);
+    q.blockDim = dim3(QG_THREADS);
+    q.dynamicSmemBytes = L.total;
+    cudaLaunchAttribute ca;
+    ca.id = cudaLaunchAttributeClusterDimension;
+    ca.val.clusterDim.x = (unsigned)g.C;
+    ca.val.clusterDim.y = 1;
+    ca.val.clusterDim.z = 1;
+    q.attrs = &ca;
+    q.numAttrs = 1;
+    int resident = 0;
+    if (cudaOccupancyMaxActiveClusters(&resident, kern, &q) != cudaSuccess || resident < ranks) {
+      cudaGetLastError();
+      return set_error(VMLX_E_UNSUPPORTED, "qgemv tp: %d ranks of %d-CTA clusters cannot be resident together",
+                       ranks, g.C);
+    }
+    if (nclu > resident / ranks) nclu = resident / ranks;
+    if (nclu < 1) nclu = 1;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(nclu * g.C), 1, 1);
+  cfg.gridDim = dim3((unsigned)(nclu * g.C), (unsigned)ranks, 1);
   cfg.blockDim = dim3(QG_THREADS);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
@@ -534,18 +613,23 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     na++;
   }
+  if (ranks > 1) {  // the ranks' CTAs wait on one another: all resident at once, or no launch
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    na = 2;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = na;
   CUtensorMap tmw;
   const uint64_t rowb = (uint64_t)a.K * BITS / 8;
-  if (!make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, rowb, (uint64_t)a.N, rowb, 128, 16,
+  if (!make_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, rowb, (uint64_t)(a.N * ranks), rowb, 128, 16,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return VMLX_E_CUDA;
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, a, g, tmw), "qgemv_kernel launch");
 }
 
 bool qgemv_covers(const QmvArgs& a, int mode, int bits, int gs) {
-  if (mode != QMV_DENSE || a.tp_world > 1) return false;
+  if (mode != QMV_DENSE) return false;
   if (a.M < 1 || a.M > QG_MAXM) return false;
   if (a.K % 8 || a.N >= (1LL << 31)) return false;
   if (!aligned(a.x, 16) || (a.norm_w && !aligned(a.norm_w, 16))) return false;
