@@ -268,7 +268,7 @@ MOE_H, MOE_E, MOE_F, MOE_K = 2048, 128, 768, 8
 MOE_EXPERT_BYTES = 3 * MOE_F * MOE_H // 2 + 3 * (MOE_F * MOE_H // 64) * 4  # gate+up+down, 4-bit g64
 
 
-def bench_moe(args, torch, vm, dev):
+def bench_moe(args, torch, vm, dev, grp=None):
     """One MoE layer for T tokens: router softmax -> top-8 of synthetic logits ~N(0,1)
     (moe_route kernel), the expert sort when T*8 >= 64 (moe_sort), SwitchGLU over the routed
     experts (gather_qmm gate||up, SwiGLU, gather_qmm down), and the score-weighted combine
@@ -290,6 +290,16 @@ def bench_moe(args, torch, vm, dev):
         layer.ensure_fused_gate_up()
         layers.append(layer)
     blocks = [vm.switch_layers.Qwen3MoESparseMoeBlock(None, L, MOE_K) for L in layers]
+    world = grp.size if grp is not None else 1
+    # TP: every expert's intermediate sharded over the group; the weighted combine and the
+    # all-reduce run as one kernel per rank (ShardedSwitchGLU -> vmlx_tp_moe_combine_all_sum)
+    sharded = [vm.distributed.ShardedSwitchGLU(L, grp) for L in layers] if world > 1 else None
+    if sharded:
+        for sL in sharded:
+            if hasattr(sL.local, "ensure_fused_gate_up"):
+                sL.local.ensure_fused_gate_up()
+        del layers[:]
+        layers.extend(range(copies))
     logits = torch.randn(T, MOE_E, device=dev, generator=g)  # router logits ~N(0,1), fp32
     inds, _ = vm.ops.moe_route(logits, MOE_K)
     x = torch.randn(T, MOE_H, device=dev, generator=g).bfloat16()
@@ -297,12 +307,19 @@ def bench_moe(args, torch, vm, dev):
 
     def layer_fn(L, xin):
         # routing (softmax + top-8), sort, SwitchGLU and the weighted combine: device kernels
+        if sharded:
+            i, sc = vm.ops.moe_route(logits, MOE_K)
+            return sharded[layers.index(L)].combined(xin, i, sc)
         return blocks[layers.index(L)](xin, logits)
     outs = [None] * copies
     calls = [(lambda i=i: outs.__setitem__(i, layer_fn(layers[i], x))) for i in range(copies)]
     with ClockSampler(dev.index or 0) as clk:
         t_layer = time_graph_calls(torch, calls, max(2, args.steps // copies), max(3, args.warmup), stream)
-    nbytes = distinct * MOE_EXPERT_BYTES + T * MOE_H * 2 * 2 + T * MOE_K * MOE_F * 2 * 3
+    if world > 1:
+        tt = torch.tensor([t_layer], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_layer = tt.item()
+    nbytes = distinct * MOE_EXPERT_BYTES // world + T * MOE_H * 2 * 2 + T * MOE_K * (MOE_F // world) * 2 * 3
     achieved = nbytes / t_layer / 1e9
 
     # end to end: pinned host tokens in, layer, host out
@@ -330,11 +347,11 @@ def bench_moe(args, torch, vm, dev):
         "value": round(T / t_layer, 2), "unit": "tokens/s", "higher_is_better": True,
         "ms_per_step": t_layer * 1e3, "dtype": "bf16",
         "config": {"workload": f"BASELINE config 4: SwitchGLU gather_qmm, hidden {MOE_H}, {MOE_E} experts, expert FFN "
-                               f"{MOE_F}, top-{MOE_K} routing from softmax of random logits, T={T} tokens, TP=1",
-                   "tokens": T, "distinct_experts": distinct, "layers_rotated": copies,
+                               f"{MOE_F}, top-{MOE_K} routing from softmax of random logits, T={T} tokens, TP={world}",
+                   "tokens": T, "parallelism": f"tp{world}", "distinct_experts": distinct, "layers_rotated": copies,
                    "l2": f"{copies} rotated layers of {MOE_E * MOE_EXPERT_BYTES / 1e6:.0f} MB of experts (> L2)",
                    "graph": "layer calls captured in a CUDA graph"},
-        "roofline": {"bound": "hbm", "kernel": "qmv_kernel gather modes (SwitchGLU gate||up and down)",
+        "roofline": {"bound": "hbm", "kernel": "gather_qmm kernels (SwitchGLU gate||up and down), per rank",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_source": peak_src, "algorithmic_bytes_per_layer": nbytes, "traffic": None},
         "e2e": {"value": round(T / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
@@ -687,8 +704,11 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if args.workload == "moe":
-        res = bench_moe(args, torch, vm, dev)
-        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "weak",
+        grp = vm.distributed.Group(strict=True) if world > 1 else None
+        res = bench_moe(args, torch, vm, dev, grp)
+        if grp is not None:
+            res["tp_status"] = grp.status()
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
                     "vs_baseline": None, "data": "synthetic (seeded random experts, router logits and tokens)"})
         if rank == 0:
             print(json.dumps(res), flush=True)
