@@ -520,7 +520,7 @@ def bench_decode(args, torch, vm, dev, rank, world, grp=None):
         "roofline": {"bound": "hbm", "kernel": "decode GEMVs (qgemv_kernel up to 8K x 8K, qmv_kernel above)", "achieved": round(gemv_achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(gemv_achieved / hbm, 4), "peak_source": peak_src,
                      "frac_of_8TBps": round(gemv_achieved / 8000, 4),
-                     "traffic": load_traffic(f"qmv_decode_B{B}_tp{world}"),
+                     "traffic": load_traffic(f"decode_gemvs_B{B}_tp{world}"),
                      "algorithmic_bytes_per_launch": int(gemv_bytes_avg), "us_per_launch": round(t_gemv * 1e6, 2)},
         "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
                 "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2},
@@ -622,7 +622,8 @@ def bench_qwen3(args, torch, vm, dev):
         "roofline": {"bound": "hbm", "kernel": "decode GEMVs (qgemv_kernel / qmv_kernel) incl. lm_head",
                      "achieved": round(gemv_bytes_avg / t_gemv / 1e9, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(gemv_bytes_avg / t_gemv / 1e9 / hbm, 4), "peak_source": peak_src,
-                     "traffic": None, "algorithmic_bytes_per_launch": int(gemv_bytes_avg),
+                     "traffic": load_traffic(f"qwen3_gemvs_B{B}_{cfg.n_layers}layers"),
+                     "algorithmic_bytes_per_launch": int(gemv_bytes_avg),
                      "us_per_launch": round(t_gemv * 1e6, 2)},
         "e2e": {"value": round(B / t_e2e, 2), "unit": "tokens/s", "ms_per_step": round(t_e2e * 1e3, 3),
                 "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
