@@ -159,6 +159,11 @@ def bench_gemv(args, torch, vm, dev):
         t_call = time_graph_calls(torch, calls, reps, max(3, args.warmup), stream)
     nbytes = gemv_bytes(M, N, K, bits, gs)
     achieved = nbytes / t_call / 1e9
+    # the reference's chained method (QuantMatmulCeilingTests.swift:52-69): 12 dependent calls, each
+    # call's output the next call's input (square matrix), weights rotated over the copies
+    bufs = [x] + [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(12)]
+    chain = [(lambda i=i: vm.quantized_mm(bufs[i], *ws[i % copies], out=bufs[i + 1])) for i in range(12)]
+    t_chain = time_graph_calls(torch, chain, max(4, args.steps // 12), 3, stream)
 
     # end to end through the public API: pinned host x -> device, call, y -> host
     xh = torch.empty(M, K, dtype=torch.bfloat16).pin_memory()
@@ -228,6 +233,9 @@ def bench_gemv(args, torch, vm, dev):
                      "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                      "frac_of_8TBps": round(achieved / 8000, 4),
                      "traffic": load_traffic("qgemv_kernel_4096x4096_b4_M1"),
+                     "chained_x12": {"us_per_call": round(t_chain * 1e6, 2),
+                                     "GBps": round(nbytes / t_chain / 1e9, 1),
+                                     "method": "12 dependent calls in one CUDA graph (output feeds the next input)"},
                      "algorithmic_bytes_per_launch": nbytes},
         "e2e": {"value": round(nbytes / t_e2e / 1e9, 2), "unit": "GB/s", "us_per_call": round(t_e2e * 1e6, 2),
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},

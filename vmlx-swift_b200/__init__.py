@@ -13,4 +13,4 @@ from .switch_layers import (QuantizedSwitchLinear, SwitchGLU, Qwen3MoESparseMoeB
                             scatter_unsort)
 from .ops import moe_combine, moe_route, moe_sort  # noqa: F401
 from . import fast, llama, qwen3  # noqa: F401,E402
-from . import distributed  # noqa: F401,E402
+from . import distributed, load  # noqa: F401,E402
