@@ -296,6 +296,28 @@ VMLX_API int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, in
 /* out = bf16(a + b), n elements (the residual adds of a decoder block). */
 VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream);
 
+/* ---- MXFP4 block-scaled weights (mode "mxfp4": group_size 32, bits 4) ---- */
+
+/*
+ * Quantize w [rows, cols] (VMLX_BF16 / VMLX_F32, cols a multiple of 32) to e2m1 codes wq
+ * (u32 [rows, cols/8], eight codes per word, low nibble first) and e8m0 scales (u8 [rows,
+ * cols/32]): scale = e8m0(max|w| / 6), code = e2m1(w / scale).  Replaces fp_quantize
+ * (Source/Cmlx/mlx-generated/metal/fp_quantized.h:1749-1789) behind mlx_quantize with mode "mxfp4".
+ */
+VMLX_API int vmlx_cuda_fp_quantize(void* wq, void* scales, const void* w, int w_dtype, int64_t rows, int64_t cols,
+                                   int group_size, int bits, const char* mode, void* stream);
+/* out [rows, cols] (VMLX_BF16 / VMLX_F32) = scale * e2m1 value, rounded once (fp_quantized.h:1791-1821). */
+VMLX_API int vmlx_cuda_fp_dequantize(void* out, int out_dtype, const void* wq, const void* scales, int64_t rows,
+                                     int64_t cols, int group_size, int bits, const char* mode, void* stream);
+/*
+ * y [M, N] bf16 = x [M, K] bf16 @ dequantize(wq [N, K/8], scales [N, K/32])^T with fp32 sums per
+ * group scaled by the group's e8m0 scale (MLX's fp qdot, fp_quantized.h:81-100) -- the
+ * mlx_quantized_matmul call of a QuantizedLinear in mode "mxfp4".
+ */
+VMLX_API int vmlx_cuda_fp_quantized_matmul(void* y, const void* x, const void* wq, const void* scales,
+                                           int group_size, int bits, const char* mode, int64_t M, int64_t N,
+                                           int64_t K, void* stream);
+
 /* ---- the decode loop around the linears (one CUDA graph per token) ---- */
 
 /*

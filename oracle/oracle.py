@@ -364,3 +364,61 @@ def ref_qmv_fast(x_bf16, wq, scales, biases, group_size=64, bits=4) -> np.ndarra
     if rc:
         raise ValueError("reference qmv_fast failed (shape not covered)")
     return y
+
+
+# ---- MXFP4 (test infrastructure: restates fp_quantize / fp_dequantize / the fp qdot of
+# Source/Cmlx/mlx-generated/metal/fp_quantized.h:81-100, 1749-1821 with fp4.h (e2m1) and
+# fp8.h:51-80 (e8m0)) ----
+
+_E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+
+
+def _e2m1_code(x: np.ndarray) -> np.ndarray:
+    """fp4_e2m1(float): the reference's threshold table (fp4.h:4-31), sign in bit 3."""
+    a = np.abs(x)
+    b = np.select([a > 5.0, a >= 3.5, a > 2.5, a >= 1.75, a > 1.25, a >= 0.75, a > 0.25],
+                  [7, 6, 5, 4, 3, 2, 1], 0).astype(np.uint32)
+    b = np.where(np.signbit(x), b | 8, b)
+    return np.where(np.isnan(x), 7, b).astype(np.uint32)
+
+
+def _e8m0(scale: np.ndarray):
+    """fp8_e8m0(float) -> (bits, value): log2 rounded half away from zero, clamped to [-127, 127];
+    bits 0 decodes to 2^-127 (fp8.h:51-80)."""
+    with np.errstate(divide="ignore"):
+        le = np.log2(scale.astype(np.float64))
+    n = np.where(scale > 0, np.sign(le) * np.floor(np.abs(le) + 0.5), -127)
+    n = np.clip(n, -127, 127).astype(np.int64)
+    bits = (n + 127).astype(np.uint32)
+    val = np.where(bits == 0, np.uint32(0x400000), bits << np.uint32(23)).astype(np.uint32).view(np.float32)
+    return bits.astype(np.uint8), val
+
+
+def mxfp4_quantize(w32: np.ndarray):
+    """float32 w [rows, cols] (bf16 inputs converted exactly) -> (u32 codes [rows, cols/8], u8 scales)."""
+    rows, cols = w32.shape
+    g = w32.reshape(rows, cols // 32, 32).astype(np.float32)
+    scale = (np.abs(g).max(-1) / np.float32(6.0)).astype(np.float32)
+    sbits, sval = _e8m0(scale)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(scale[..., None] == 0, np.float32(0), (g / sval[..., None]).astype(np.float32))
+    codes = _e2m1_code(q).reshape(rows, cols // 8, 8)
+    words = np.zeros((rows, cols // 8), np.uint32)
+    for i in range(8):
+        words |= codes[..., i] << np.uint32(4 * i)
+    return words, sbits
+
+
+def mxfp4_values(wq: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """Exact float32 values scale * e2m1 of every code: [rows, cols]."""
+    rows = wq.shape[0]
+    codes = np.stack([(wq >> np.uint32(4 * i)) & np.uint32(0xF) for i in range(8)], -1).reshape(rows, -1)
+    v = _E2M1[codes & 7] * np.where(codes & 8, -1.0, 1.0).astype(np.float32)
+    s = np.where(scales == 0, np.uint32(0x400000), scales.astype(np.uint32) << np.uint32(23)).astype(
+        np.uint32).view(np.float32)
+    return (v.reshape(rows, -1, 32) * s[..., None]).reshape(rows, -1).astype(np.float32)
+
+
+def mxfp4_qmm_f64(x_bf16, wq, scales) -> np.ndarray:
+    """x [M, K] (bf16 bits) @ (mxfp4 values)^T in float64."""
+    return bf16_to_f32(x_bf16).astype(np.float64) @ mxfp4_values(wq, scales).astype(np.float64).T

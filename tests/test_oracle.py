@@ -116,3 +116,21 @@ def test_gather_sort_permutations(orc):
     assert list(sidx) == [0, 1, 1, 2, 3, 3]
     assert list(order) == [3, 1, 2, 5, 0, 4]  # stable
     assert np.array_equal(sidx[inv], idx.reshape(-1))
+
+
+def test_mxfp4_oracle_known_answers(orc):
+    """Hand-computed groups: max 6 -> scale 1 (e8m0 127), values on the grid map to their codes,
+    midpoints go to the even mantissa (0.25 -> 0, 0.75 -> 1.0, 1.25 -> 1.0, 2.5 -> 2.0, 5 -> 4.0);
+    an all-zero group gets the smallest scale (bits 0) and zero codes; max 3 -> scale 0.5 (126)."""
+    import numpy as np
+    g = np.array([6, -3, 0.5, 0.25, 0.75, 1.25, 2.5, 5] + [0] * 24, np.float32)
+    w = np.stack([g, np.zeros(32, np.float32), g / 2]).astype(np.float32)
+    wq, sc = orc.mxfp4_quantize(w)
+    assert sc.ravel().tolist() == [127, 0, 126]
+    codes = [(int(wq[0, 0]) >> (4 * i)) & 0xF for i in range(8)]
+    assert codes == [7, 8 | 5, 1, 0, 2, 2, 4, 6]
+    assert wq[1].tolist() == [0, 0, 0, 0]
+    assert np.array_equal(wq[2], wq[0])  # the same codes at half the scale
+    v = orc.mxfp4_values(wq, sc)
+    assert v[0, :8].tolist() == [6.0, -3.0, 0.5, 0.0, 1.0, 1.0, 2.0, 4.0]
+    assert v[2, 0] == 3.0

@@ -200,14 +200,16 @@ def quantized_modules(weights: Dict[str, torch.Tensor], paths: Iterable[str], pl
         mode = q.mode
         if f"{base}.biases" in weights and mode in ("mxfp4", "mxfp8"):
             mode = "affine"  # an MXFP stamp over an affine payload: load it as affine
-        if mode != "affine":
-            raise VMLXError(VMLX_E_UNSUPPORTED, f"{path}: quantization mode {mode!r} (affine only)")
+        if mode not in ("affine", "mxfp4"):
+            raise VMLXError(VMLX_E_UNSUPPORTED, f"{path}: quantization mode {mode!r} (affine, mxfp4)")
         w, s = weights[f"{base}.weight"], weights[f"{base}.scales"]
         bq = weights.get(f"{base}.biases")
         bias = weights.get(f"{base}.bias")
         if w.shape[-1] * 32 // q.bits != s.shape[-1] * q.group_size:
             raise VMLXError(VMLX_E_INVALID, f"{path}: packed width {w.shape[-1]} does not match "
                                             f"{q.bits}-bit groups of {q.group_size} ({s.shape[-1]} groups)")
+        if mode == "mxfp4" and (w.dim() != 2 or path.endswith("embed_tokens")):
+            raise VMLXError(VMLX_E_UNSUPPORTED, f"{path}: mxfp4 is supported for dense linears only")
         if path.endswith("embed_tokens"):
             out[path] = (w, s, bq, q.group_size, q.bits)
         elif w.dim() == 3:

@@ -22,8 +22,8 @@ class QuantizedLinear:
     def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor], scales: torch.Tensor,
                  biases: Optional[torch.Tensor], group_size: int = 64, bits: int = 4,
                  mode: str = "affine"):
-        if mode != "affine":
-            raise ops.VMLXError(2, f"mode {mode} not supported")
+        if mode not in ("affine", "mxfp4"):
+            raise ops.VMLXError(2, f"mode {mode} not supported (affine, mxfp4)")
         self.weight = weight
         self.bias = bias
         self.scales = scales
@@ -35,6 +35,9 @@ class QuantizedLinear:
     @classmethod
     def from_weight(cls, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
                     group_size: int = 64, bits: int = 4, mode: str = "affine") -> "QuantizedLinear":
+        if mode == "mxfp4":  # e2m1 codes with e8m0 scales per 32 values, no biases
+            wq, s = ops.fp_quantized(weight, group_size=group_size, bits=bits, mode=mode)
+            return cls(wq, bias, s, None, group_size, bits, mode)
         wq, s, b = ops.quantized(weight, group_size=group_size, bits=bits, mode=mode)
         return cls(wq, bias, s, b, group_size, bits, mode)
 
@@ -55,8 +58,11 @@ class QuantizedLinear:
                 f"bias={'true' if self.bias is not None else 'false'})")
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        y = ops.quantized_mm(x, self.weight, self.scales, self.biases, transpose=True,
-                             group_size=self.group_size, bits=self.bits, mode=self.mode, out=out)
+        if self.mode == "mxfp4":
+            y = ops.fp_quantized_mm(x, self.weight, self.scales, self.group_size, self.bits, self.mode, out=out)
+        else:
+            y = ops.quantized_mm(x, self.weight, self.scales, self.biases, transpose=True,
+                                 group_size=self.group_size, bits=self.bits, mode=self.mode, out=out)
         if self.bias is not None:
             y = y + self.bias
         return y

@@ -256,3 +256,43 @@ def moe_combine(y: torch.Tensor, scores: torch.Tensor, inverse_order: Optional[t
 
 def gather_qmm_workspace_size(batch: int, M: int, K: int, n_experts: int) -> int:
     return int(_lib.lib().vmlx_cuda_gather_qmm_workspace_size(batch, M, K, n_experts))
+
+
+# ---- MXFP4 (mode "mxfp4": e2m1 codes, one e8m0 scale per 32 values, no biases) ----
+
+def fp_quantized(w: torch.Tensor, group_size: int = 32, bits: int = 4, mode: str = "mxfp4"):
+    """w [..., K] (bf16 / f32) -> (wq int32 [..., K/8] holding u32 words, scales uint8 [..., K/32])."""
+    _need_cuda(w)
+    w = w.contiguous()
+    K = w.shape[-1]
+    rows = w.numel() // K
+    wq = torch.empty(*w.shape[:-1], K // 8, dtype=torch.int32, device=w.device)
+    sc = torch.empty(*w.shape[:-1], K // 32, dtype=torch.uint8, device=w.device)
+    check(_lib.lib().vmlx_cuda_fp_quantize(wq.data_ptr(), sc.data_ptr(), w.data_ptr(), _dtype_code(w.dtype), rows, K,
+                                           group_size, bits, mode.encode(), _stream(w)))
+    return wq, sc
+
+
+def fp_dequantized(wq: torch.Tensor, scales: torch.Tensor, group_size: int = 32, bits: int = 4,
+                   mode: str = "mxfp4", dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    _need_cuda(wq, scales)
+    K = wq.shape[-1] * 8
+    rows = wq.numel() * 8 // K
+    out = torch.empty(*wq.shape[:-1], K, dtype=dtype, device=wq.device)
+    check(_lib.lib().vmlx_cuda_fp_dequantize(out.data_ptr(), _dtype_code(dtype), wq.data_ptr(), scales.data_ptr(), rows,
+                                             K, group_size, bits, mode.encode(), _stream(wq)))
+    return out
+
+
+def fp_quantized_mm(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, group_size: int = 32, bits: int = 4,
+                    mode: str = "mxfp4", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need_cuda(x, wq, scales)
+    x = x.contiguous()
+    K = x.shape[-1]
+    N = wq.shape[-2]
+    M = x.numel() // K
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    check(_lib.lib().vmlx_cuda_fp_quantized_matmul(out.data_ptr(), x.data_ptr(), wq.data_ptr(), scales.data_ptr(),
+                                                   group_size, bits, mode.encode(), M, N, K, _stream(x)))
+    return out
