@@ -295,6 +295,9 @@ VMLX_API int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, in
 
 /* out = bf16(a + b), n elements (the residual adds of a decoder block). */
 VMLX_API int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream);
+/* out[r, c] = bf16(y[r, c] + bias[c]), rows x cols bf16: the optional bias of QuantizedLinear
+ * (Source/MLXNN/Quantized.swift:361-376).  out may alias y. */
+VMLX_API int vmlx_cuda_bias_add(void* out, const void* y, const void* bias, int64_t rows, int64_t cols, void* stream);
 
 /* ---- MXFP4 block-scaled weights (mode "mxfp4": group_size 32, bits 4) ---- */
 

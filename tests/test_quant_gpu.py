@@ -327,3 +327,16 @@ def test_launch_overlap_chain_matches(vm, orc, cuda):
     finally:
         lib.vmlx_set_launch_overlap(prev)
     assert torch.equal(ref, got)
+
+
+def test_quantized_linear_bias(vm, orc, cuda):
+    """QuantizedLinear with a bias: bf16(bf16(x @ W^T) + bias), the bias added on the device."""
+    g = torch.Generator(cuda).manual_seed(9)
+    w = (torch.randn(320, 512, device=cuda, generator=g) * 0.02).bfloat16()
+    bias = torch.randn(320, device=cuda, generator=g).bfloat16()
+    ql = vm.QuantizedLinear.from_weight(w, bias=bias)
+    for M in (1, 7):
+        x = torch.randn(M, 512, device=cuda, generator=g).bfloat16()
+        y = ql(x)
+        ref = (vm.quantized_mm(x, ql.weight, ql.scales, ql.biases).float() + bias.float()).bfloat16()
+        assert torch.equal(y, ref)

@@ -64,6 +64,7 @@ SIGNATURES = {
                                              _c.c_float, _vp]),
     "vmlx_cuda_silu_mul": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "vmlx_cuda_bias_add": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "vmlx_cuda_fp_quantize": (_int, [_vp, _vp, _vp, _int, _i64, _i64, _int, _int, _str, _vp]),
     "vmlx_cuda_fp_dequantize": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _int, _int, _str, _vp]),
     "vmlx_cuda_fp_quantized_matmul": (_int, [_vp, _vp, _vp, _vp, _int, _int, _str, _i64, _i64, _i64, _vp]),

@@ -401,6 +401,13 @@ __global__ void add_kernel(const bf16* __restrict__ a, const bf16* __restrict__ 
     out[i] = __float2bfloat16_rn(__bfloat162float(a[i]) + __bfloat162float(b[i]));
 }
 
+// out[r, c] = bf16(y[r, c] + bias[c]): the bias of a QuantizedLinear (Quantized.swift:361-376).
+__global__ void bias_add_kernel(const bf16* __restrict__ y, const bf16* __restrict__ bias, bf16* __restrict__ out,
+                                int64_t n, int64_t cols) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2bfloat16_rn(__bfloat162float(y[i]) + __bfloat162float(bias[i % cols]));
+}
+
 }  // namespace vmlx
 
 using namespace vmlx;
@@ -567,6 +574,16 @@ extern "C" int vmlx_cuda_silu_mul(void* out, const void* gate_up, int64_t rows, 
   silu_mul_kernel<<<grid_for(rows * ffn, 256), 256, 0, as_stream(stream)>>>((const bf16*)gate_up, (bf16*)out, rows,
                                                                            (int)ffn);
   return check_launch("vmlx_cuda_silu_mul");
+}
+
+extern "C" int vmlx_cuda_bias_add(void* out, const void* y, const void* bias, int64_t rows, int64_t cols,
+                                  void* stream) {
+  if (!out || !y || !bias) return set_error(VMLX_E_INVALID, "bias_add: null pointer");
+  if (rows < 0 || cols <= 0) return set_error(VMLX_E_INVALID, "bias_add: bad shape");
+  if (rows == 0) return VMLX_OK;
+  bias_add_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>((const bf16*)y, (const bf16*)bias,
+                                                                            (bf16*)out, rows * cols, cols);
+  return check_launch("vmlx_cuda_bias_add");
 }
 
 extern "C" int vmlx_cuda_add(void* out, const void* a, const void* b, int64_t n, void* stream) {

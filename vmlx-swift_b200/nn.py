@@ -63,6 +63,8 @@ class QuantizedLinear:
         else:
             y = ops.quantized_mm(x, self.weight, self.scales, self.biases, transpose=True,
                                  group_size=self.group_size, bits=self.bits, mode=self.mode, out=out)
-        if self.bias is not None:
-            y = y + self.bias
+        if self.bias is not None:  # the bias add on the device, in place (bf16(y + bias))
+            cols = y.shape[-1]
+            ops.check(ops._lib.lib().vmlx_cuda_bias_add(y.data_ptr(), y.data_ptr(), self.bias.contiguous().data_ptr(),
+                                                        y.numel() // cols, cols, ops._stream(y)))
         return y
