@@ -94,11 +94,12 @@ def _shards(vm, cuda, world, N, K, gs, bits, seed):
     return parts, stacked
 
 
-@pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("M", [1, 4, 9, 32])
-def test_loopback_row_parallel_linear(vm, orc, cuda, world, M):
+@pytest.mark.parametrize("world,M,N,K", [(w, m, 1024, 2048) for w in (2, 4) for m in (1, 4, 9, 32)] +
+                         [(8, 1, 4096, 4096), (8, 4, 4096, 14336)])
+def test_loopback_row_parallel_linear(vm, orc, cuda, world, M, N, K):
+    """world 8 with the Llama o_proj / down_proj shards of TP=8 (K 512 / 1792 per rank)."""
     lib = vm.lib()
-    N, K, gs, bits = 1024, 2048, 64, 4
+    gs, bits = 64, 4
     kr = K // world
     parts, (wst, sst, bst) = _shards(vm, cuda, world, N, K, gs, bits, 11 + M)
     g = torch.Generator(device=cuda).manual_seed(M)
