@@ -641,7 +641,8 @@ bool qgemv_covers(const QmvArgs& a, int mode, int bits, int gs) {
   (void)gs;
   const int force = env_cached(0);
   if (force >= 0) return force != 0;
-  return a.N >= 1024 && a.N <= 8192 && a.K <= 8192;
+  // (5120 x 8192, the Qwen3-32B o_proj: 13.8 us here against 11.9 us on the other kernel)
+  return a.N >= 1024 && a.N <= 8192 && a.K <= 8192 && a.N * a.K <= (32LL << 20);
 }
 
 template <int GS>
