@@ -30,6 +30,11 @@
 //  * Tokens are the MMA's N dimension (8 per tile, up to 4 tiles = 32 rows).
 // Each row's result does not depend on M (batch invariance, as the
 // reference's QuantizedSmallMScalingBenchTests.swift:110-127 requires).
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "kernels.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
@@ -744,6 +749,67 @@ qmv_kernel(QmvArgs p, const __grid_constant__ CUtensorMap tmw, const __grid_cons
   if (!ok && p.status) atomicExch(p.status, VMLX_E_STATE);
 }
 
+// The kernel instance a launch of launch_qmv_bg will use (its template arguments do not
+// depend on the cluster size), for occupancy queries.
+template <int BITS, int GS, int NT, bool CC>
+static const void* qmv_fn(bool tp) {
+  return tp ? (const void*)qmv_kernel<BITS, GS, NT, CC, true> : (const void*)qmv_kernel<BITS, GS, NT, CC, false>;
+}
+template <int BITS, int GS>
+static const void* qmv_kernel_for(int toka, bool cc, bool tp) {
+  if constexpr (BITS == 4) {
+    if (cc) {
+      switch (toka) {
+        case 1: return qmv_fn<BITS, GS, 1, true>(tp);
+        case 2: return qmv_fn<BITS, GS, 2, true>(tp);
+        case 3: return qmv_fn<BITS, GS, 3, true>(tp);
+        default: return qmv_fn<BITS, GS, 4, true>(tp);
+      }
+    }
+  }
+  switch ((toka + 7) / 8) {
+    case 1: return qmv_fn<BITS, GS, 1, false>(tp);
+    case 2: return qmv_fn<BITS, GS, 2, false>(tp);
+    case 3: return qmv_fn<BITS, GS, 3, false>(tp);
+    default: return qmv_fn<BITS, GS, 4, false>(tp);
+  }
+}
+
+// Clusters of C CTAs (with `smem` dynamic shared memory) that can be resident at once: the
+// GPCs must hold whole clusters, so e.g. 7-CTA clusters leave SMs of every GPC idle.  Cached.
+static int qmv_resident_clusters(const void* fn, int C, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(fn, C, smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (ensure_max_dynamic_smem(fn, 226 * 1024)) return 0;
+  cudaLaunchConfig_t q = {};
+  q.gridDim = dim3((unsigned)C, 1, 1);
+  q.blockDim = dim3(QMV_THREADS);
+  q.dynamicSmemBytes = smem;
+  cudaLaunchAttribute ca;
+  ca.id = cudaLaunchAttributeClusterDimension;
+  ca.val.clusterDim.x = (unsigned)C;
+  ca.val.clusterDim.y = 1;
+  ca.val.clusterDim.z = 1;
+  q.attrs = &ca;
+  q.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &q) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
 template <int BITS, int GS, int NT, bool CC, bool TP>
 static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int C, int toka, cudaStream_t st) {
   auto kern = qmv_kernel<BITS, GS, NT, CC, TP>;
@@ -779,6 +845,10 @@ static int launch_qmv_k(const QmvArgs& a, int mode, int64_t zcount, int ks, int 
   // A loopback group runs every rank's grid in one launch: the ranks share the SMs.
   const int ranks = (TP && a.tp_loop) ? a.tp_world : 1;
   int64_t max_clusters = (int64_t)sm_count() * per_sm / C / ranks;
+  {  // no more clusters than can be resident at once (the grid is persistent)
+    const int res = qmv_resident_clusters((const void*)kern, C, L.total);
+    if (res > 0 && max_clusters > res / ranks) max_clusters = res / ranks;
+  }
   if (max_clusters < 1) max_clusters = 1;
   if (ranks > 1) {  // clusters of C CTAs that can be resident at once, shared by the ranks
     cudaLaunchConfig_t q = {};
@@ -856,6 +926,7 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
   // 4-bit with <= QMV_CC_MAX_TOKENS token rows: the CUDA-core consumer (fewer
   // instructions per weight than an m16n8 MMA that would be mostly empty)
   const bool cc = BITS == 4 && toka <= QMV_CC_MAX_TOKENS;
+  const void* kfn = qmv_kernel_for<BITS, GS>(toka, cc, a.tp_world > 1);
   auto smem_of = [&](int ks_, int toka_) {
     QmvPlan L;
     L.init(BITS, GS, ks_, toka_, cc);
@@ -875,7 +946,9 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     int reg_cap = cc ? 2 : 3;  // 160 threads x ~150 (CUDA-core) / ~128 (MMA) registers
     if (reg_cap > QMV_MAX_PER_SM) reg_cap = QMV_MAX_PER_SM;
     per_sm = per_sm > reg_cap ? reg_cap : (per_sm < 1 ? 1 : per_sm);
-    const int64_t clusters = (int64_t)sm_count() * per_sm / C;
+    int64_t clusters = (int64_t)sm_count() * per_sm / C;
+    const int res = qmv_resident_clusters(kfn, C, sm);
+    if (res > 0 && res < clusters) clusters = res;
     if (clusters < 1) continue;
     // each item also pays a fixed cost (x / scale staging, pipeline fill, the
     // cluster reduction) worth roughly 8 groups of streaming
@@ -883,6 +956,10 @@ static int launch_qmv_bg(const QmvArgs& a, int mode, int64_t zcount, int toka, c
     if (cost < best) { best = cost; bestC = C; }
   }
   int C = bestC;
+  {  // tuning override (read once): VMLX_QMV_C forces the cluster size when it is valid
+    static const int forceC = [] { const char* v = getenv("VMLX_QMV_C"); return v && *v ? atoi(v) : 0; }();
+    if (forceC >= 1 && forceC <= QMV_MAX_CLUSTER && forceC <= KG) C = forceC;
+  }
 
   int ks = slice_groups(KG, C, SG);
   while (smem_of(ks, toka) > 226 * 1024 && toka > 8) toka -= 8;
