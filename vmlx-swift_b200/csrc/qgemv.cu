@@ -42,6 +42,9 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace vmlx {
 
@@ -518,6 +521,44 @@ static void qg_fill(QgGeom& gm, int64_t N, int64_t K, int gs, int S, int C) {
 // stages per warp, plus a fixed cost per tile and per cluster reduction) against the
 // bandwidth share of the resident CTAs; shared memory is sized for the regime's largest
 // M so that the geometry never depends on M.
+// Clusters of C CTAs that can be resident at once for this geometry's shared memory (whole
+// clusters per GPC), queried on one instance of the kernel (the geometry must not depend on M).
+static int qg_resident_clusters(int gs, int C, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(gs, C, smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const void* fn = gs == 32 ? (const void*)qgemv_kernel<32, 4>
+                 : gs == 64 ? (const void*)qgemv_kernel<64, 4> : (const void*)qgemv_kernel<128, 4>;
+  int n = 0;
+  if (!ensure_max_dynamic_smem(fn, 220 * 1024)) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3((unsigned)C, 1, 1);
+    q.blockDim = dim3(QG_THREADS);
+    q.dynamicSmemBytes = smem;
+    cudaLaunchAttribute ca;
+    ca.id = cudaLaunchAttributeClusterDimension;
+    ca.val.clusterDim.x = (unsigned)C;
+    ca.val.clusterDim.y = 1;
+    ca.val.clusterDim.z = 1;
+    q.attrs = &ca;
+    q.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &q) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
 static bool qg_choose(int64_t N, int64_t K, int bits, int gs, QgGeom& best) {
   const int64_t KG = K / gs;
   const int GC = 128 / (gs * bits / 8);
@@ -540,7 +581,11 @@ static bool qg_choose(int64_t N, int64_t K, int bits, int gs, QgGeom& best) {
       if (L.total > 200 * 1024) continue;
       const int per_sm = qg_per_sm(L);
       if (per_sm < 1) continue;
-      const int64_t nclu = std::min<int64_t>(gm.ntiles, (int64_t)sms * per_sm / C);
+      int64_t nclu = std::min<int64_t>(gm.ntiles, (int64_t)sms * per_sm / C);
+      {
+        const int res = qg_resident_clusters(gs, C, L.total);
+        if (res > 0 && res < nclu) nclu = res;
+      }
       if (nclu < 1) continue;
       const int64_t tiles_per = (gm.ntiles + nclu - 1) / nclu;
       const double stages = (double)tiles_per * (gm.GW / GC);           // per warp, serial
@@ -574,6 +619,12 @@ static int launch_qg(const QmvArgs& a, cudaStream_t st) {
   // A loopback TP group runs every rank's grid in one launch: the ranks share the SMs.
   const int ranks = (a.tp_world > 1 && a.tp_loop) ? a.tp_world : 1;
   int64_t nclu = std::min<int64_t>(g.ntiles, (int64_t)sm_count() * qg_per_sm(L, MT) / g.C / ranks);
+  {
+    QgSmem L4;
+    L4.init(g, QG_MAXM);
+    const int res = qg_resident_clusters(GS, g.C, L4.total);
+    if (res > 0 && nclu > res / ranks) nclu = std::max<int64_t>(1, res / ranks);
+  }
   if (a.tp_world > 1) {
     // every CTA waits for the other ranks after its own rows: the whole grid must be resident
     cudaLaunchConfig_t q = {};
